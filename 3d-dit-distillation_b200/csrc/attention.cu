@@ -1,0 +1,501 @@
+// Non-causal varlen flash attention on Blackwell tensor cores (tcgen05 + TMEM + TMA).
+//
+// One CTA computes a 128-query tile of one head of one segment.  Warp roles:
+//   warp 0      TMA producer: Q once, then K/V tiles (128 keys) into a 2-stage ring
+//   warp 1      MMA issuer (one elected thread): S = Q K^T into a double-buffered
+//               TMEM accumulator, O += P V into a TMEM accumulator
+//   warps 2..5  softmax group: one query row per thread; reads S from TMEM,
+//               online softmax in fp32 (exp2), writes P (bf16) to shared memory,
+//               rescales O in TMEM only when the running max grew by more than
+//               2^8 (exact: the final O/l uses the same reference max), and runs
+//               the epilogue (O / l -> bf16 -> global, optional row scatter).
+// Shared-memory operands use the canonical UMMA layouts: Q/K K-major with 64-byte
+// swizzle (TMA boxes of 32 channels), V MN-major with 64-byte swizzle, P K-major
+// with 128-byte swizzle.  No cluster multicast is used anywhere.
+// Every mbarrier wait is bounded; a wait that runs out records an error in
+// g_device_error, raises a CTA abort flag and the CTA skips to its teardown.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <math.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace vdit {
+
+__device__ int g_device_error = 0;
+
+namespace fmha {
+
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int STAGES = 2;
+constexpr int THREADS = 192;
+constexpr int MAXSEG = 128;
+constexpr uint32_t kSpinLimit = 1u << 22;   // try_wait polls before a wait is declared stuck
+constexpr int kErrTimeout = 0x4154;   // "AT"
+
+struct SegInfo {
+    int nseg;
+    int q0[MAXSEG + 1];
+    int k0[MAXSEG + 1];
+    int tile0[MAXSEG + 1];
+};
+
+// ---------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// bounded wait; false when the CTA aborted (ours or another thread's timeout)
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+    }
+    *abort_flag = 1;
+    atomicExch(&g_device_error, kErrTimeout);
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
+// 32 lanes x 32 consecutive fp32 columns -> 32 registers per thread
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+    uint32_t r[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i]);
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+          "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+          "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Shared-memory matrix descriptors (sm_100 format: start>>4 in [0,14), LBO>>4 in
+// [16,30), SBO>>4 in [32,46), version 1 at bit 46, layout type in [61,64)).
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint64_t layout) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (layout << 61);
+}
+constexpr uint64_t kSw128 = 2, kSw64 = 4;
+
+// instruction descriptor: f32 accumulate, bf16 A/B, A K-major, B K- or MN-major
+__host__ __device__ constexpr uint32_t make_idesc(int m, int n, bool b_mn_major) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
+           ((uint32_t)(m >> 4) << 24);
+}
+
+// ---------------------------------------------------------------- kernel
+template <int HD>
+__global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
+                                                              const __grid_constant__ CUtensorMap tmK,
+                                                              const __grid_constant__ CUtensorMap tmV,
+                                                              __nv_bfloat16* __restrict__ out, int64_t out_stride,
+                                                              const int64_t* __restrict__ out_rows,
+                                                              const __grid_constant__ SegInfo seg, float scale_log2) {
+    constexpr int NCH = HD / 32;                 // 64-byte channel chunks per row
+    constexpr int CHUNK = BM * 64;               // bytes of one chunk of a 128-row tile
+    constexpr int TILE = NCH * CHUNK;            // bytes of one 128-row Q/K/V tile
+    constexpr int PBYTES = BM * BN * 2;
+    constexpr uint32_t IDESC_QK = make_idesc(BM, BN, false);
+    constexpr uint32_t IDESC_PV = make_idesc(BM, HD, true);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = sQ + TILE;
+    uint8_t* sV = sK + STAGES * TILE;
+    uint8_t* sP = sV + STAGES * TILE;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + PBYTES);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t b_q = smem_u32(&bars[0]);
+    auto b_kvfull = [&](int s) { return smem_u32(&bars[1 + s]); };
+    auto b_kvempty = [&](int s) { return smem_u32(&bars[3 + s]); };
+    auto b_sfull = [&](int s) { return smem_u32(&bars[5 + s]); };
+    auto b_sempty = [&](int s) { return smem_u32(&bars[7 + s]); };
+    const uint32_t b_pfull = smem_u32(&bars[9]);
+    const uint32_t b_pvdone = smem_u32(&bars[10]);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int head = blockIdx.y;
+    const int tile = blockIdx.x;
+    int s = 0;
+    while (s + 1 < seg.nseg && seg.tile0[s + 1] <= tile) ++s;
+    const int q_row0 = seg.q0[s] + (tile - seg.tile0[s]) * BM;
+    const int q_rows = min(BM, seg.q0[s + 1] - q_row0);
+    const int k_begin = seg.k0[s];
+    const int k_len = seg.k0[s + 1] - k_begin;
+    const int n_kv = (k_len + BN - 1) / BN;
+
+    if (n_kv == 0) {   // empty key set: output zeros (uniform for the CTA, before any barrier)
+        for (int r = threadIdx.x; r < q_rows; r += THREADS) {
+            const int64_t orow = out_rows ? out_rows[q_row0 + r] : (int64_t)(q_row0 + r);
+            for (int c = 0; c < HD; ++c) out[orow * out_stride + (int64_t)head * HD + c] = f2bf(0.f);
+        }
+        return;
+    }
+
+    if (threadIdx.x == 0) {
+        mbar_init(b_q, 1);
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(b_kvfull(i), 1);
+            mbar_init(b_kvempty(i), 1);
+            mbar_init(b_sfull(i), 1);
+            mbar_init(b_sempty(i), 128);
+        }
+        mbar_init(b_pfull, 128);
+        mbar_init(b_pvdone, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmQ)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmK)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmV)) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tmem_O = tmem + 2 * BN;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            mbar_expect_tx(b_q, TILE);
+            for (int c = 0; c < NCH; ++c) tma_load_3d(smem_u32(sQ + c * CHUNK), &tmQ, c * 32, head, q_row0, b_q);
+            for (int j = 0; j < n_kv; ++j) {
+                const int st = j & 1;
+                if (j >= STAGES && !mbar_wait(b_kvempty(st), ((j - STAGES) >> 1) & 1, abort_flag)) break;
+                mbar_expect_tx(b_kvfull(st), 2 * TILE);
+                const int krow = k_begin + j * BN;
+                for (int c = 0; c < NCH; ++c)
+                    tma_load_3d(smem_u32(sK + st * TILE + c * CHUNK), &tmK, c * 32, head, krow, b_kvfull(st));
+                for (int c = 0; c < NCH; ++c)
+                    tma_load_3d(smem_u32(sV + st * TILE + c * CHUNK), &tmV, c * 32, head, krow, b_kvfull(st));
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            bool ok = mbar_wait(b_q, 0, abort_flag);
+            auto issue_pv = [&](int t) -> bool {
+                if (!mbar_wait(b_pfull, t & 1, abort_flag)) return false;
+                tc_fence_after();
+                const int stv = t & 1;
+                const uint32_t pbase = smem_u32(sP), vbase = smem_u32(sV + stv * TILE);
+#pragma unroll
+                for (int kk = 0; kk < BN / 16; ++kk) {
+                    const uint64_t a = make_desc(pbase + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024, kSw128);
+                    const uint64_t b = make_desc(vbase + kk * 16 * 64, CHUNK, 512, kSw64);
+                    tc_mma(tmem_O, a, b, IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
+                }
+                tc_commit(b_pvdone);
+                tc_commit(b_kvempty(stv));
+                return true;
+            };
+            for (int j = 0; ok && j < n_kv; ++j) {
+                const int st = j & 1;
+                if (!mbar_wait(b_kvfull(st), (j >> 1) & 1, abort_flag)) { ok = false; break; }
+                if (j >= 2 && !mbar_wait(b_sempty(st), ((j - 2) >> 1) & 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t qbase = smem_u32(sQ), kbase = smem_u32(sK + st * TILE);
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk) {
+                    const uint32_t off = (kk >> 1) * CHUNK + (kk & 1) * 32;
+                    const uint64_t a = make_desc(qbase + off, 16, 512, kSw64);
+                    const uint64_t b = make_desc(kbase + off, 16, 512, kSw64);
+                    tc_mma(tmem + st * BN, a, b, IDESC_QK, kk > 0 ? 1u : 0u);
+                }
+                tc_commit(b_sfull(st));
+                if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+            }
+            if (ok) issue_pv(n_kv - 1);
+        }
+    } else {
+        // ------------------------------------------------------------ softmax group
+        const int quarter = warp & 3;                    // TMEM lane quarter this warp may access
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+        float m_run = -INFINITY, l_run = 0.f;
+        bool ok = true;
+        uint8_t* prow = sP + row * 128;
+        for (int j = 0; j < n_kv; ++j) {
+            const int st = j & 1;
+            // every lane runs each wait, then the warp agrees, so an abort never splits the warp
+            ok = __all_sync(0xffffffffu, mbar_wait(b_sfull(st), (j >> 1) & 1, abort_flag));
+            if (!ok) break;
+            tc_fence_after();
+            float sv[BN];
+#pragma unroll
+            for (int c = 0; c < BN / 32; ++c) tmem_ld32(tmem + lane_off + st * BN + c * 32, sv + c * 32);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(b_sempty(st));
+            const int valid = min(BN, k_len - j * BN);
+            float mt = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < BN; ++c) {
+                if (c >= valid) sv[c] = -INFINITY;
+                mt = fmaxf(mt, sv[c]);
+            }
+            const float m_new = fmaxf(m_run, mt * scale_log2);
+            if (j > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(b_pvdone, (j - 1) & 1, abort_flag));
+                if (!ok) break;
+                tc_fence_after();
+            }
+            float alpha = 1.f;
+            bool rescale = false;
+            if (j == 0) {
+                m_run = m_new;
+            } else if (m_new > m_run + 8.f) {
+                alpha = ex2(m_run - m_new);
+                m_run = m_new;
+                l_run *= alpha;
+                rescale = true;
+            }
+            if (__any_sync(0xffffffffu, rescale)) {      // warp-uniform TMEM round trip
+#pragma unroll 1
+                for (int c = 0; c < HD / 32; ++c) {
+                    float ov[32];
+                    tmem_ld32(tmem_O + lane_off + c * 32, ov);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+                    tmem_st32(tmem_O + lane_off + c * 32, ov);
+                }
+                tmem_wait_st();
+            }
+            // P = exp2(S*scale - m) as bf16 into the 128B-swizzled K-major tile
+            float lsum = 0.f;
+#pragma unroll
+            for (int q = 0; q < BN / 8; ++q) {
+                float p[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    p[i] = ex2(fmaf(sv[q * 8 + i], scale_log2, -m_run));
+                    lsum += p[i];
+                }
+                const int region = q >> 3, lc = q & 7;
+                *reinterpret_cast<uint4*>(prow + region * (BM * 128) + ((lc ^ (row & 7)) << 4)) = pack8(p);
+            }
+            l_run += lsum;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            mbar_arrive(b_pfull);
+        }
+        // ------------------------------------------------------------ epilogue
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(b_pvdone, (n_kv - 1) & 1, abort_flag));
+        if (ok) {
+            tc_fence_after();
+            const float inv = 1.f / l_run;
+            const bool live = row < q_rows;
+            const int64_t orow = live ? (out_rows ? out_rows[q_row0 + row] : (int64_t)(q_row0 + row)) : 0;
+            __nv_bfloat16* dst = out + orow * out_stride + (int64_t)head * HD;
+#pragma unroll 1
+            for (int c = 0; c < HD / 32; ++c) {
+                float ov[32];
+                tmem_ld32(tmem_O + lane_off + c * 32, ov);
+                tmem_wait_ld();
+                if (live) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) ov[i] *= inv;
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) = pack8(ov + v * 8);
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+    }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int heads, int hd, int64_t row_stride) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)heads, (cuuint64_t)rows};
+    cuuint64_t strides[2] = {(cuuint64_t)hd * 2, (cuuint64_t)row_stride * 2};
+    cuuint32_t box[3] = {32, 1, (cuuint32_t)BM};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int HD>
+size_t smem_bytes() {
+    return 1024 + (size_t)HD * 256 * (1 + 2 * STAGES) + (size_t)BM * BN * 2 + 128;
+}
+
+template <int HD>
+int launch(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, __nv_bfloat16* out, int64_t out_stride,
+           const int64_t* out_rows, const SegInfo& seg, int tiles, int heads, float scale_log2, cudaStream_t s) {
+    static bool configured = false;
+    const size_t sm = smem_bytes<HD>();
+    if (!configured) {
+        if (cudaFuncSetAttribute(fmha_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+            return VDIT_ERR_LAUNCH;
+        configured = true;
+    }
+    fmha_fwd_kernel<HD><<<dim3(tiles, heads), THREADS, sm, s>>>(q, k, v, out, out_stride, out_rows, seg, scale_log2);
+    return VDIT_OK;
+}
+
+}  // namespace fmha
+}  // namespace vdit
+
+using namespace vdit;
+
+extern "C" int vdit_attention(const void* q, int64_t q_stride, const void* k, int64_t k_stride, const void* v,
+                              int64_t v_stride, void* out, int64_t out_stride, const int64_t* out_rows,
+                              const int32_t* cu_q, const int32_t* cu_k, int32_t nseg, int32_t heads, int32_t hd,
+                              float scale, vdit_stream_t stream) {
+    using namespace vdit::fmha;
+    if (!q || !k || !v || !out || !cu_q || !cu_k || nseg < 1 || heads < 1) return VDIT_ERR_ARG;
+    if (nseg > MAXSEG) return VDIT_ERR_UNSUPPORTED;
+    if (hd != 96 && hd != 128) return VDIT_ERR_UNSUPPORTED;
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || q_stride % 8 || k_stride % 8 ||
+        v_stride % 8 || out_stride % 8)
+        return VDIT_ERR_ALIGN;
+    if (q_stride < (int64_t)heads * hd || k_stride < (int64_t)heads * hd || v_stride < (int64_t)heads * hd ||
+        out_stride < (int64_t)heads * hd)
+        return VDIT_ERR_ARG;
+    SegInfo seg;
+    memset(&seg, 0, sizeof(seg));
+    seg.nseg = nseg;
+    int tiles = 0;
+    for (int i = 0; i <= nseg; ++i) {
+        if (cu_q[i] < 0 || cu_k[i] < 0) return VDIT_ERR_ARG;
+        if (i > 0 && (cu_q[i] < cu_q[i - 1] || cu_k[i] < cu_k[i - 1])) return VDIT_ERR_ARG;
+        seg.q0[i] = cu_q[i];
+        seg.k0[i] = cu_k[i];
+        seg.tile0[i] = tiles;
+        if (i < nseg) tiles += (cu_q[i + 1] - cu_q[i] + BM - 1) / BM;
+    }
+    if (tiles == 0) return VDIT_OK;
+    const int64_t q_rows = cu_q[nseg], k_rows = cu_k[nseg];
+    CUtensorMap mq, mk, mv;
+    if (!make_map(&mq, q, q_rows, heads, hd, q_stride) || !make_map(&mk, k, k_rows, heads, hd, k_stride) ||
+        !make_map(&mv, v, k_rows, heads, hd, v_stride))
+        return VDIT_ERR_DRIVER;
+    const float scale_log2 = scale * 1.4426950408889634f;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+    int rc = hd == 128 ? launch<128>(mq, mk, mv, o, out_stride, out_rows, seg, tiles, heads, scale_log2, s)
+                       : launch<96>(mq, mk, mv, o, out_stride, out_rows, seg, tiles, heads, scale_log2, s);
+    if (rc != VDIT_OK) return rc;
+    count_launches(1);
+    return check_launch();
+}
+
+extern "C" int vdit_device_error(int clear) {
+    int v = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess) return VDIT_ERR_LAUNCH;
+    if (cudaMemcpyFromSymbol(&v, vdit::g_device_error, sizeof(int)) != cudaSuccess) return VDIT_ERR_LAUNCH;
+    if (clear) {
+        int z = 0;
+        if (cudaMemcpyToSymbol(vdit::g_device_error, &z, sizeof(int)) != cudaSuccess) return VDIT_ERR_LAUNCH;
+    }
+    return v;
+}

@@ -1,0 +1,336 @@
+"""Host wrappers of the sm_100a kernels, under the reference's ``lib/fast_kernels.py`` names.
+
+Each function allocates its outputs with torch (device memory is torch's
+caching allocator), launches on the current CUDA stream through the C ABI
+and raises on any error.  There is no CPU or Triton path.
+
+Reference names kept: ``precompute_rope_3d_table``, ``precompute_rope_2d_cond``,
+``build_order_caches_fast``, ``build_conv_indices_fast``, ``fast_sparse_conv3d``,
+``fast_modulate``, ``fast_gate_add_and_modulate``, ``fast_gate_add``,
+``fused_qknorm_rope3d_gather``, ``fused_qknorm_rope2d_cond_inplace``,
+``fast_swiglu_from_packed``, ``fast_out_modulate_unpatchify``,
+``flash_varlen_qkvpacked_already_sorted``, ``flash_cross_attn``,
+``flash_cond_self_attn``.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from ._lib import check, lib, ptr, stream_of
+
+BF16 = torch.bfloat16
+
+
+def _s(t: torch.Tensor) -> int:
+    return stream_of(t)
+
+
+def _f32(v: torch.Tensor) -> torch.Tensor:
+    return v.reshape(-1).to(torch.float32).contiguous()
+
+
+# ----------------------------------------------------------------------------- geometry
+
+def lex_perm(vox: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(perm, up_widx, h_coords) of one sample, ``lib/fast_flow.py:667-694``."""
+    vox = vox.to(torch.int32).contiguous()
+    n = vox.shape[0]
+    dev = vox.device
+    perm = torch.empty(n, dtype=torch.int64, device=dev)
+    up = torch.empty(n, dtype=torch.int64, device=dev)
+    hc = torch.empty(n, 4, dtype=torch.int32, device=dev)
+    ws = torch.empty(int(lib().vdit_geometry_workspace_bytes(n)), dtype=torch.uint8, device=dev)
+    check(lib().vdit_lex_perm(ptr(vox), n, ptr(perm), ptr(up), ptr(hc), ptr(ws), ws.numel(), _s(vox)), "lex_perm")
+    return perm, up, hc
+
+
+def hilbert4_orders(h_coords: torch.Tensor, coord_bound: int, return_codes: bool = False):
+    """Codes and (fwd, bwd) permutations of the orders (h, ht1, h1, ht)."""
+    h_coords = h_coords.to(torch.int32).contiguous()
+    n = h_coords.shape[0]
+    dev = h_coords.device
+    fwd = torch.empty(4, n, dtype=torch.int64, device=dev)
+    bwd = torch.empty(4, n, dtype=torch.int64, device=dev)
+    codes = torch.empty(4, n, dtype=torch.int64, device=dev) if return_codes else None
+    ws = torch.empty(int(lib().vdit_geometry_workspace_bytes(n)), dtype=torch.uint8, device=dev)
+    check(lib().vdit_hilbert4_orders(ptr(h_coords), n, int(coord_bound), ptr(codes), ptr(fwd), ptr(bwd), ptr(ws),
+                                     ws.numel(), _s(h_coords)), "hilbert4_orders")
+    return (codes, fwd, bwd) if return_codes else (fwd, bwd)
+
+
+def window_seqlens(sizes: Sequence[int], patch_size: int) -> Tuple[List[int], int]:
+    """Host-side window partition, ``lib/fast_kernels.py:1764-1790``."""
+    lens: List[int] = []
+    for s in sizes:
+        s = int(s)
+        if s > 0:
+            full = (s - 1) // patch_size
+            lens += [patch_size] * full + [s - full * patch_size]
+    cu = [0]
+    for v in lens:
+        cu.append(cu[-1] + v)
+    return cu, (max(lens) if lens else 0)
+
+
+def build_order_caches_fast(h_coords: torch.Tensor, sizes: List[int], orders: Sequence[str], order_kwargs: dict,
+                            seqlen_cache: Optional[dict] = None, arange_n: Optional[torch.Tensor] = None,
+                            use_triton: bool = True, coord_bound: Optional[int] = None):
+    """Four Hilbert window orders of one sample -> [(fwd, bwd, cu_seqlens, max_len)] * 4
+    (``lib/fast_kernels.py:1739-1836``; ``use_triton`` is accepted and ignored).
+    ``cu_seqlens`` is returned as a device int32 tensor carrying a host copy in
+    ``.host`` (the attention launch needs the window sizes on the host)."""
+    if tuple(orders) != ("h", "ht1", "h1", "ht"):
+        raise NotImplementedError(f"orders {tuple(orders)}: only ('h', 'ht1', 'h1', 'ht') is built")
+    if len(sizes) != 1:
+        raise NotImplementedError("one sample per geometry")
+    patch = int(order_kwargs.get("patch_size", 4096))
+    cu, max_len = window_seqlens(sizes, patch)
+    if coord_bound is None:
+        coord_bound = int(h_coords[:, 1:].max().item()) + 1 if h_coords.numel() else 1
+    fwd, bwd = hilbert4_orders(h_coords, coord_bound)
+    cu_t = torch.tensor(cu, dtype=torch.int32, device=h_coords.device)
+    cu_t.host = cu
+    return [(fwd[i], bwd[i], cu_t, max_len) for i in range(4)]
+
+
+def build_conv_indices_fast(coords: torch.Tensor, already_sorted: bool = False) -> List[torch.Tensor]:
+    """27-neighbour indices [N,27] int32 (-1 absent), ``lib/fast_kernels.py:1649-1701``."""
+    coords = coords.to(torch.int32).contiguous()
+    n = coords.shape[0]
+    if already_sorted:
+        out = torch.empty(n, 27, dtype=torch.int32, device=coords.device)
+        check(lib().vdit_conv_indices(ptr(coords), n, ptr(out), _s(coords)), "conv_indices")
+        return [out]
+    if n and int(coords[:, 0].max().item()) != 0:
+        raise NotImplementedError("unsorted coordinates of several samples")
+    perm, up, hc = lex_perm(coords[:, 1:].contiguous())
+    sorted_idx = build_conv_indices_fast(hc, already_sorted=True)[0]
+    # rows back to input order, neighbour ids back to input ids
+    idx = sorted_idx[up]
+    out = torch.where(idx >= 0, perm[idx.clamp(min=0).long()].to(torch.int32), idx)
+    return [out.contiguous()]
+
+
+def precompute_rope_3d_table(res: int = 64, base: float = 128.0, head_dim: int = 96,
+                             device: Optional[torch.device] = None):
+    """[res, head_dim//6] cos/sin (fp64 -> fp32), ``lib/fast_kernels.py:977-993``."""
+    m = head_dim // 6
+    c = torch.empty(res, m, dtype=torch.float32, device=device)
+    s = torch.empty_like(c)
+    check(lib().vdit_rope3d_table(res, head_dim, float(base), ptr(c), ptr(s), _s(c)), "rope3d_table")
+    return c, s
+
+
+def precompute_rope_2d_cond(cond_size: int = 64, base: float = 64.0, head_dim: int = 96,
+                            device: Optional[torch.device] = None):
+    """[cond_size^2, 2, head_dim//4] cos/sin, ``lib/fast_kernels.py:1011-1035``."""
+    m = head_dim // 4
+    c = torch.empty(cond_size * cond_size, 2, m, dtype=torch.float32, device=device)
+    s = torch.empty_like(c)
+    check(lib().vdit_rope2d_table(cond_size, head_dim, float(base), ptr(c), ptr(s), _s(c)), "rope2d_table")
+    return c, s
+
+
+# ----------------------------------------------------------------------------- row kernels
+
+def patchify(xt: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """x = xt @ w^T, xt [N,16] fp32, w [D,16] fp32 -> bf16 [N,D]."""
+    xt = xt.to(torch.float32).contiguous()
+    out = torch.empty(xt.shape[0], w.shape[0], dtype=BF16, device=xt.device)
+    check(lib().vdit_patchify(ptr(xt), xt.shape[0], ptr(w), w.shape[0], ptr(out), _s(xt)), "patchify")
+    return out
+
+
+def fast_modulate(x: torch.Tensor, sizes, scale1: torch.Tensor, shift: torch.Tensor,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """LN(x) * scale1 + shift; ``scale1`` is 1 + scale (fp32 [D])."""
+    m, d = x.shape
+    out = torch.empty_like(x) if out is None else out
+    check(lib().vdit_modulate(ptr(x), m, d, ptr(scale1), ptr(shift), ptr(out), _s(x)), "modulate")
+    return out
+
+
+def fast_gate_add_and_modulate(x: torch.Tensor, h: torch.Tensor, gate: torch.Tensor,
+                               scale1: Optional[torch.Tensor], shift: Optional[torch.Tensor],
+                               out: Optional[torch.Tensor] = None, broadcast_h: bool = False):
+    """x += h * gate in place; returns LN(x) * scale1 + shift (or None when scale1 is None).
+    ``broadcast_h`` adds one [D] row of h to every row of x."""
+    m, d = x.shape
+    mod = None
+    if scale1 is not None:
+        mod = torch.empty_like(x) if out is None else out
+    stride = 0 if broadcast_h else h.stride(0)
+    check(lib().vdit_gate_add_modulate(ptr(x), ptr(h), stride, m, d, ptr(gate), ptr(scale1), ptr(shift), ptr(mod),
+                                       _s(x)), "gate_add_modulate")
+    return mod
+
+
+def fast_gate_add(x: torch.Tensor, h: torch.Tensor, gate: torch.Tensor, broadcast_h: bool = False) -> torch.Tensor:
+    fast_gate_add_and_modulate(x, h, gate, None, None, broadcast_h=broadcast_h)
+    return x
+
+
+def fast_out_modulate_unpatchify(x: torch.Tensor, sizes, scale1: torch.Tensor, shift: torch.Tensor,
+                                 w_fp32: torch.Tensor) -> torch.Tensor:
+    """[N,16] fp32 = bf16(LN(x)*scale1+shift) @ w^T (``lib/fast_kernels.py:888-940``)."""
+    m, d = x.shape
+    out = torch.empty(m, w_fp32.shape[0], dtype=torch.float32, device=x.device)
+    check(lib().vdit_out_modulate_unpatchify(ptr(x), m, d, ptr(scale1), ptr(shift), ptr(w_fp32), ptr(out), _s(x)),
+          "out_modulate_unpatchify")
+    return out
+
+
+def fused_qknorm_rope3d_gather(qkv: torch.Tensor, q_scale: torch.Tensor, k_scale: torch.Tensor,
+                               cos_t: torch.Tensor, sin_t: torch.Tensor, h_coords: torch.Tensor,
+                               fwd_idx: Optional[torch.Tensor], heads: int, head_dim: int,
+                               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Hilbert-gathered [N,3,H,HD]: RoPE3D(RMS(q)*qs), RoPE3D(RMS(k)*ks), v
+    (``lib/fast_kernels.py:1476-1535``)."""
+    n = qkv.shape[0]
+    out = torch.empty(n, 3 * heads * head_dim, dtype=BF16, device=qkv.device) if out is None else out
+    check(lib().vdit_qknorm_rope3d_gather(ptr(qkv), n, heads, head_dim, ptr(q_scale), ptr(k_scale), ptr(cos_t),
+                                          ptr(sin_t), cos_t.shape[0], ptr(h_coords), ptr(fwd_idx), ptr(out), _s(qkv)),
+          "qknorm_rope3d_gather")
+    return out
+
+
+def fused_qknorm_rope2d_cond_inplace(qkv: torch.Tensor, q_scale: torch.Tensor, k_scale: torch.Tensor,
+                                     cos2d: torch.Tensor, sin2d: torch.Tensor, heads: int, head_dim: int,
+                                     n_prefix: int = 5) -> torch.Tensor:
+    """Context tokens in place: RMS(q,k)*scale, 2D RoPE on tokens >= 5
+    (``lib/fast_kernels.py:1412-1473``)."""
+    l = qkv.shape[0]
+    check(lib().vdit_qknorm_rope2d(ptr(qkv), l, heads, head_dim, ptr(q_scale), ptr(k_scale), ptr(cos2d), ptr(sin2d),
+                                   n_prefix, _s(qkv)), "qknorm_rope2d")
+    return qkv
+
+
+def fast_swiglu_from_packed(h_packed: torch.Tensor) -> torch.Tensor:
+    """silu(h[:, F:]) * h[:, :F] (``lib/fast_kernels.py:942-974``)."""
+    m, f2 = h_packed.shape
+    out = torch.empty(m, f2 // 2, dtype=BF16, device=h_packed.device)
+    check(lib().vdit_swiglu_packed(ptr(h_packed), m, f2 // 2, ptr(out), _s(h_packed)), "swiglu_packed")
+    return out
+
+
+def fast_sparse_conv3d(feat: torch.Tensor, weight_fp32: torch.Tensor, bias_fp32: torch.Tensor,
+                       conv_indices, fuse_swiglu: bool = False) -> torch.Tensor:
+    """Depthwise 27-tap conv (``lib/fast_kernels.py:1704-1736``); with
+    ``fuse_swiglu`` returns silu(y[:, C/2:]) * y[:, :C/2]."""
+    idx = conv_indices[0] if isinstance(conv_indices, (list, tuple)) else conv_indices
+    n, c = feat.shape
+    out = torch.empty(n, c // 2 if fuse_swiglu else c, dtype=BF16, device=feat.device)
+    check(lib().vdit_dwconv27(ptr(feat), n, c, ptr(idx), ptr(weight_fp32), ptr(bias_fp32), ptr(out),
+                              1 if fuse_swiglu else 0, _s(feat)), "dwconv27")
+    return out
+
+
+def dense_sparse_conv3d(feat: torch.Tensor, weight_t_bf16: torch.Tensor, bias_fp32: torch.Tensor,
+                        conv_indices) -> torch.Tensor:
+    """Dense 27-tap sparse conv (``BK/ops/sparse.py:84-123``); ``weight_t_bf16`` is
+    [27, C_out, C_in] (the reference (3,3,3,C_in,C_out) weight transposed)."""
+    idx = conv_indices[0] if isinstance(conv_indices, (list, tuple)) else conv_indices
+    n, cin = feat.shape
+    cout = weight_t_bf16.shape[1]
+    out = torch.empty(n, cout, dtype=BF16, device=feat.device)
+    check(lib().vdit_dense_conv27(ptr(feat), n, cin, cout, ptr(idx), ptr(weight_t_bf16), ptr(bias_fp32), ptr(out),
+                                  _s(feat)), "dense_conv27")
+    return out
+
+
+# ----------------------------------------------------------------------------- attention
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_q: Sequence[int], cu_k: Sequence[int],
+              heads: int, head_dim: int, out: Optional[torch.Tensor] = None,
+              out_rows: Optional[torch.Tensor] = None, scale: Optional[float] = None) -> torch.Tensor:
+    """Varlen non-causal attention on tcgen05.  q/k/v are 2D views [rows, >=H*HD]
+    (any row stride); ``cu_q``/``cu_k`` are host lists of segment offsets;
+    ``out_rows`` scatters output row i to out_rows[i]."""
+    if out is None:
+        out = torch.empty(q.shape[0], heads * head_dim, dtype=BF16, device=q.device)
+    nseg = len(cu_q) - 1
+    cq, ck = _host_i32(cu_q), _host_i32(cu_k)      # host arrays, alive for the call
+    scale = 1.0 / math.sqrt(head_dim) if scale is None else scale
+    check(lib().vdit_attention(ptr(q), q.stride(0), ptr(k), k.stride(0), ptr(v), v.stride(0), ptr(out), out.stride(0),
+                               ptr(out_rows), ctypes.addressof(cq), ctypes.addressof(ck), nseg, heads, head_dim,
+                               float(scale), _s(q)), "attention")
+    return out
+
+
+def _host_i32(vals: Sequence[int]):
+    return (ctypes.c_int32 * len(vals))(*[int(v) for v in vals])
+
+
+def flash_varlen_qkvpacked_already_sorted(qkv_sorted: torch.Tensor, cu_seqlens, max_len: int, heads: int,
+                                          head_dim: int, out_rows: Optional[torch.Tensor] = None,
+                                          out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Window self-attention over Hilbert-sorted packed qkv [N, 3*H*HD]
+    (``lib/fast_kernels.py:1538-1587``); ``out_rows`` = fwd index scatters the
+    result back to voxel order (fusing ``out[bwd_idx]``)."""
+    d = heads * head_dim
+    cu = getattr(cu_seqlens, "host", None) or [int(v) for v in cu_seqlens.tolist()]
+    return attention(qkv_sorted[:, :d], qkv_sorted[:, d:2 * d], qkv_sorted[:, 2 * d:], cu, cu, heads, head_dim,
+                     out=out, out_rows=out_rows)
+
+
+def flash_cross_attn(q: torch.Tensor, cu_q, max_q: int, kv: torch.Tensor, cu_k, max_k: int, heads: int,
+                     head_dim: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Cross attention, q [Nq, H*HD], kv [Nk, 2*H*HD] packed (``lib/fast_kernels.py:1605-1646``)."""
+    d = heads * head_dim
+    cq = getattr(cu_q, "host", None) or [int(v) for v in (cu_q.tolist() if torch.is_tensor(cu_q) else cu_q)]
+    ck = getattr(cu_k, "host", None) or [int(v) for v in (cu_k.tolist() if torch.is_tensor(cu_k) else cu_k)]
+    return attention(q, kv[:, :d], kv[:, d:2 * d], cq, ck, heads, head_dim, out=out)
+
+
+def flash_cond_self_attn(qkv_cond: torch.Tensor, heads: int, head_dim: int,
+                         out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Full self-attention over the context tokens, packed [L, 3*H*HD]
+    (``lib/fast_kernels.py:1590-1602``)."""
+    d = heads * head_dim
+    l = qkv_cond.shape[0]
+    return attention(qkv_cond[:, :d], qkv_cond[:, d:2 * d], qkv_cond[:, 2 * d:], [0, l], [0, l], heads, head_dim,
+                     out=out)
+
+
+def attention_1q(q: torch.Tensor, kv: torch.Tensor, heads: int, head_dim: int,
+                 k_offset: int = 0, v_offset: Optional[int] = None) -> torch.Tensor:
+    """One query per head ([H*HD]) over the rows of ``kv`` (K at column
+    ``k_offset``, V at ``v_offset``): the 1-token context->x attention
+    (``lib/fast_flow.py:1769-1777``)."""
+    d = heads * head_dim
+    v_offset = k_offset + d if v_offset is None else v_offset
+    n = kv.shape[0]
+    ws = torch.empty(int(lib().vdit_attention_1q_workspace_bytes(heads, head_dim, n)), dtype=torch.uint8,
+                     device=kv.device)
+    out = torch.empty(d, dtype=BF16, device=kv.device)
+    q = q.reshape(-1).to(BF16).contiguous()
+    check(lib().vdit_attention_1q(ptr(q), ptr(kv[:, k_offset:]), ptr(kv[:, v_offset:]), kv.stride(0), n, heads,
+                                  head_dim, float(1.0 / math.sqrt(head_dim)), ptr(out), ptr(ws), ws.numel(), _s(kv)),
+          "attention_1q")
+    return out
+
+
+# ----------------------------------------------------------------------------- sampler glue
+
+def gather_rows_f32(src: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    src = src.to(torch.float32).contiguous()
+    out = torch.empty(idx.shape[0], src.shape[1], dtype=torch.float32, device=src.device)
+    check(lib().vdit_gather_rows_f32(ptr(src), ptr(idx), idx.shape[0], src.shape[1], ptr(out), _s(src)), "gather_rows")
+    return out
+
+
+def cfg_euler_(xt: torch.Tensor, v_pos: torch.Tensor, v_neg: Optional[torch.Tensor], guidance: float, dt: float):
+    check(lib().vdit_cfg_euler(ptr(xt), ptr(v_pos), ptr(v_neg), xt.shape[0], float(guidance), float(dt), _s(xt)),
+          "cfg_euler")
+    return xt
+
+
+def unpermute_denorm(xt: torch.Tensor, up_widx: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor) -> torch.Tensor:
+    out = torch.empty_like(xt)
+    check(lib().vdit_unpermute_denorm(ptr(xt), ptr(up_widx), xt.shape[0], ptr(scale), ptr(shift), ptr(out), _s(xt)),
+          "unpermute_denorm")
+    return out

@@ -1,0 +1,180 @@
+/*
+ * vdit.h -- C ABI of the B200 (sm_100a) sparse-voxel DiT (lat_dit) forward path.
+ *
+ * Conventions
+ *  - Every entry point returns VDIT_OK (0) or a negative VDIT_ERR_* code and
+ *    never throws.  Shapes are checked on the host before any launch.
+ *  - The caller owns every buffer: inputs, outputs and workspaces are device
+ *    pointers allocated by the caller; the library keeps no pointer past
+ *    return.  "bf16" buffers are IEEE bfloat16, row-major, contiguous along
+ *    the last dimension; strides are in elements.
+ *  - All work is enqueued on `stream` (a cudaStream_t passed as void*); calls
+ *    are asynchronous and reentrant.
+ *  - Citations name the reference interface each entry point replaces
+ *    (paths relative to the reference project; BK/ = baseline_repo/3dgen-main/).
+ */
+#ifndef VDIT_H_
+#define VDIT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* vdit_stream_t;
+
+#define VDIT_OK 0
+#define VDIT_ERR_ARG (-1)          /* bad shape / size / null pointer        */
+#define VDIT_ERR_ALIGN (-2)        /* pointer or stride not 16-byte aligned  */
+#define VDIT_ERR_LAUNCH (-3)       /* CUDA launch error                      */
+#define VDIT_ERR_UNSUPPORTED (-4)  /* head_dim / width not supported         */
+#define VDIT_ERR_WORKSPACE (-5)    /* workspace too small                    */
+#define VDIT_ERR_DRIVER (-6)       /* driver entry point (tensor maps) failed */
+
+/* ------------------------------------------------------------------ runtime */
+const char* vdit_version(void);
+const char* vdit_error_string(int code);
+/* Number of kernels this library has launched since load (all devices). */
+long long vdit_launch_count(void);
+/* Device error word of the current device (a bounded wait that ran out or an
+ * index out of range seen by a kernel).  Synchronizes the device; clear!=0
+ * resets the word.  Returns 0 when no error was recorded. */
+int vdit_device_error(int clear);
+
+/* ------------------------------------------------------------------ geometry */
+/* Workspace (bytes) for vdit_lex_perm / vdit_hilbert4_orders on n voxels. */
+size_t vdit_geometry_workspace_bytes(int64_t n);
+
+/* SparseDownsample(patch=1) order of one sample.  Replaces the key/argsort
+ * block of _prepare_sample_geometry (lib/fast_flow.py:667-694) and
+ * BK/base_models/sparse.py:998-1036.  vox [n,3] int32 (0 <= c < 1024, unique);
+ * writes perm [n] int64, up_widx [n] int64 (inverse) and h_coords [n,4]
+ * int32 = (0, vox[perm]). */
+int vdit_lex_perm(const int32_t* vox, int64_t n, int64_t* perm, int64_t* up_widx,
+                  int32_t* h_coords, void* workspace, size_t workspace_bytes,
+                  vdit_stream_t stream);
+
+/* Four Hilbert window orders (h, ht1, h1, ht) of one sample.  Replaces
+ * _encode_hilbert_4_kernel + argsort in build_order_caches_fast
+ * (lib/fast_kernels.py:1126-1154, 1792-1822; semantics BK/base_models/order.py:6-111).
+ * h_coords [n,4] int32; coord_bound = exclusive upper bound of x,y,z (res).
+ * Writes codes4 [4,n] int64 (may be NULL), fwd4 [4,n] int64, bwd4 [4,n] int64. */
+int vdit_hilbert4_orders(const int32_t* h_coords, int64_t n, int32_t coord_bound,
+                         int64_t* codes4, int64_t* fwd4, int64_t* bwd4,
+                         void* workspace, size_t workspace_bytes, vdit_stream_t stream);
+
+/* 27-neighbour submanifold index table.  Replaces libsparse.conv_indices
+ * (BK/ops/libsparse/libsparse.cpp:29-37, conv.cu:21-163).  h_coords [n,4]
+ * int32 must be sorted lexicographically by (b,x,y,z) (the output of
+ * vdit_lex_perm); writes out [n,27] int32, -1 where the neighbour is absent. */
+int vdit_conv_indices(const int32_t* h_coords, int64_t n, int32_t* out, vdit_stream_t stream);
+
+/* RoPE tables in fp64 rounded to fp32.  Replace precompute_rope_3d_table /
+ * precompute_rope_2d_cond (lib/fast_kernels.py:977-1035).
+ * 3D: cos/sin [res, head_dim/6].  2D: cos/sin [cond_size^2, 2, head_dim/4]. */
+int vdit_rope3d_table(int32_t res, int32_t head_dim, double base, float* cos_out, float* sin_out,
+                      vdit_stream_t stream);
+int vdit_rope2d_table(int32_t cond_size, int32_t head_dim, double base, float* cos_out,
+                      float* sin_out, vdit_stream_t stream);
+
+/* ------------------------------------------------------------------ row kernels */
+/* x[n,d] bf16 = xt[n,16] fp32 @ w[d,16]^T (patchify, lib/fast_flow.py:931-935). */
+int vdit_patchify(const float* xt, int64_t n, const float* w, int32_t d, void* x_out,
+                  vdit_stream_t stream);
+
+/* out = LN(x) * scale1 + shift with scale1 = 1 + scale (fast_modulate,
+ * lib/fast_kernels.py:672-885; BK/models/generators/lat_dit.py:63-66).
+ * x, out bf16 [m,d]; scale1, shift fp32 [d]; d % 8 == 0, d <= 2048. */
+int vdit_modulate(const void* x, int64_t m, int32_t d, const float* scale1, const float* shift,
+                  void* out, vdit_stream_t stream);
+
+/* x <- x + h * gate (in place, bf16) and, when mod_out != NULL,
+ * mod_out = LN(x) * scale1 + shift.  h_row_stride 0 broadcasts one row of h.
+ * Replaces _fused_gate_add_ln_modulate_kernel (lib/fast_kernels.py:556-611). */
+int vdit_gate_add_modulate(void* x, const void* h, int64_t h_row_stride, int64_t m, int32_t d,
+                           const float* gate, const float* scale1, const float* shift,
+                           void* mod_out, vdit_stream_t stream);
+
+/* out[m,16] fp32 = bf16(LN(x) * scale1 + shift) @ w[16,d]^T.  Replaces
+ * _fused_out_modulate_unpatchify_kernel (lib/fast_kernels.py:613-648, 888-940). */
+int vdit_out_modulate_unpatchify(const void* x, int64_t m, int32_t d, const float* scale1,
+                                 const float* shift, const float* w, float* out,
+                                 vdit_stream_t stream);
+
+/* out[j] = (RoPE3D(RMS(q[src])*q_scale), RoPE3D(RMS(k[src])*k_scale), v[src]),
+ * src = fwd[j] (NULL: identity).  qkv/out bf16 [n,3,heads,head_dim];
+ * q_scale/k_scale fp32 [heads,head_dim]; cos/sin fp32 [res, head_dim/6];
+ * h_coords [n,4] int32 (coordinates of input rows, < res).  Replaces
+ * _fused_qknorm_rope3d_gather_kernel (lib/fast_kernels.py:1156-1303, 1476-1535). */
+int vdit_qknorm_rope3d_gather(const void* qkv, int64_t n, int32_t heads, int32_t head_dim,
+                              const float* q_scale, const float* k_scale, const float* cos_t,
+                              const float* sin_t, int32_t res, const int32_t* h_coords,
+                              const int64_t* fwd, void* out, vdit_stream_t stream);
+
+/* Context tokens, in place: q,k <- RMS(.)*scale, then 2D RoPE on tokens
+ * >= n_prefix using cos/sin [l - n_prefix, 2, head_dim/4].  Replaces
+ * _fused_qknorm_rope2d_cond_inplace_kernel (lib/fast_kernels.py:1305-1473). */
+int vdit_qknorm_rope2d(void* qkv, int64_t l, int32_t heads, int32_t head_dim, const float* q_scale,
+                       const float* k_scale, const float* cos2d, const float* sin2d,
+                       int32_t n_prefix, vdit_stream_t stream);
+
+/* out[m,f] = silu(h[:, f:2f]) * h[:, :f] from packed h [m,2f] bf16.  Replaces
+ * _fused_packed_swiglu_kernel (lib/fast_kernels.py:650-669, 942-974). */
+int vdit_swiglu_packed(const void* h, int64_t m, int32_t f, void* out, vdit_stream_t stream);
+
+/* Depthwise 27-tap submanifold conv: y[n,c] = b[c] + sum_d w[d,c] h[idx[n,d],c]
+ * with fp32 weights/accumulation.  fuse_swiglu=0: out bf16 [n,c];
+ * fuse_swiglu=1: out bf16 [n,c/2] = silu(y[:, c/2:]) * y[:, :c/2] with y
+ * rounded to bf16 first.  Replaces libsparse.conv_fwd (BK/ops/libsparse/conv.cu:187-309,
+ * libsparse.cpp:40-56) and, fused, the SwiGLU that follows it
+ * (BK/models/generators/lat_dit.py:477-484). */
+int vdit_dwconv27(const void* h, int64_t n, int32_t c, const int32_t* idx, const float* w,
+                  const float* b, void* out, int32_t fuse_swiglu, vdit_stream_t stream);
+
+/* ------------------------------------------------------------------ attention */
+/* Non-causal varlen flash attention on tcgen05 tensor cores (head_dim 96 or 128).
+ * Row i of segment s attends to key rows [cu_k[s], cu_k[s+1]).  q/k/v point at
+ * head 0 of row 0; row r head h lives at ptr + r*stride + h*head_dim (bf16).
+ * out row for query row i is out_rows[i] when out_rows != NULL (scatter), else i.
+ * cu_q_host/cu_k_host are HOST int32 arrays [nseg+1], nseg <= 128.
+ * Replaces flash_attn varlen (qkv/kv packed) calls: sparse_windowed_sdp /
+ * sparse_cross_sdp (BK/base_models/sparse.py:834-896), flash_varlen_qkvpacked_already_sorted,
+ * flash_cond_self_attn, flash_cross_attn (lib/fast_kernels.py:1538-1646). */
+int vdit_attention(const void* q, int64_t q_stride, const void* k, int64_t k_stride, const void* v,
+                   int64_t v_stride, void* out, int64_t out_stride, const int64_t* out_rows,
+                   const int32_t* cu_q_host, const int32_t* cu_k_host, int32_t nseg,
+                   int32_t heads, int32_t head_dim, float softmax_scale, vdit_stream_t stream);
+
+/* Workspace bytes for vdit_attention_1q over n_keys keys. */
+size_t vdit_attention_1q_workspace_bytes(int32_t heads, int32_t head_dim, int64_t n_keys);
+
+/* One query per head over n_keys keys (the exact 1-token uncond context->x
+ * attention, lib/fast_flow.py:1769-1777).  q [heads,head_dim] bf16; k/v rows
+ * at k + r*kv_stride + h*head_dim; out [heads,head_dim] bf16.  Split-K with
+ * partials in the caller's workspace. */
+int vdit_attention_1q(const void* q, const void* k, const void* v, int64_t kv_stride,
+                      int64_t n_keys, int32_t heads, int32_t head_dim, float softmax_scale,
+                      void* out, void* workspace, size_t workspace_bytes, vdit_stream_t stream);
+
+/* ------------------------------------------------------------------ sampler glue */
+/* dst[j,:] = src[idx[j],:] for fp32 rows of width c (noise[perm], lib/fast_flow.py:2576). */
+int vdit_gather_rows_f32(const float* src, const int64_t* idx, int64_t n, int32_t c, float* dst,
+                         vdit_stream_t stream);
+
+/* CFG + Euler step on [n,16] fp32 (lib/fast_flow.py:2836,2887,3288):
+ * v = v_pos + g*(v_pos - v_neg) (v_neg NULL: v = v_pos); xt -= dt * v. */
+int vdit_cfg_euler(float* xt, const float* v_pos, const float* v_neg, int64_t n, float guidance,
+                   float dt, vdit_stream_t stream);
+
+/* out[i,:] = xt[up_widx[i],:] * scale + shift, 16 channels (unpermute +
+ * denormalize, lib/fast_flow.py:3306-3313). */
+int vdit_unpermute_denorm(const float* xt, const int64_t* up_widx, int64_t n, const float* scale,
+                          const float* shift, float* out, vdit_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VDIT_H_ */

@@ -1,0 +1,110 @@
+"""CPU tests: the C-ABI library loads and exports every declared symbol, and
+the host-side logic (schedule, solver config, plugin contract, window
+partition, architecture/keys) matches the oracle/reference behaviour."""
+import json
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import vdit
+from vdit import _lib
+from vdit import fast_kernels as fk
+from vdit.fast_sampler import SolverConfig, build_schedule
+from vdit.model import LatDitArch, param_shapes
+from vdit.runtime import FlowMatchSamplingParams, LatDitGenerator, resolve
+
+from oracle import geometry as geo
+from oracle import model as om
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _declared():
+    text = (ROOT / "include" / "vdit.h").read_text()
+    return sorted(set(re.findall(r"\b(vdit_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = _declared()
+    assert len(names) >= 20
+    for n in names:
+        assert hasattr(lib, n), n
+    assert set(names) == set(_lib.SIGNATURES), set(names) ^ set(_lib.SIGNATURES)
+
+
+def test_error_strings_and_host_queries():
+    lib = _lib.load()
+    assert b"sm_100a" in lib.vdit_version()
+    for code in (0, -1, -2, -3, -4, -5, -6):
+        assert lib.vdit_error_string(code)
+    assert lib.vdit_launch_count() >= 0
+    assert lib.vdit_attention_1q_workspace_bytes(12, 128, 16384) > 0
+    assert lib.vdit_attention_1q_workspace_bytes(0, 128, 16384) == 0
+
+
+def test_shape_errors_are_reported_before_any_launch():
+    lib = _lib.load()
+    # null pointers / bad shapes are rejected on the host (no GPU needed)
+    assert lib.vdit_modulate(None, 10, 1536, None, None, None, None) == -1
+    assert lib.vdit_attention(None, 0, None, 0, None, 0, None, 0, None, None, None, 0, 12, 128, 1.0, None) == -1
+    assert lib.vdit_dwconv27(None, 5, 7680, None, None, None, None, 1, None) == -1
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        _lib.check(-1, "probe")
+
+
+@pytest.mark.parametrize("steps,guided", [(4, 3), (8, 6), (14, None)])
+def test_build_schedule_matches_oracle(steps, guided):
+    cfg = SolverConfig(num_inference_steps=steps, n_guided_steps=guided or 10,
+                       n_unguided_steps=(steps - guided) if guided else 4)
+    t, g, ng = build_schedule(cfg)
+    if guided:
+        to, go = om.build_schedule(steps, guided, 3.0, (0.5, 1.0))
+        assert torch.allclose(t, to) and g == go and ng == guided
+    assert t[0] == 1.0 and t[-1] == 0.0 and len(g) == steps
+
+
+def test_solver_config_reads_json_and_ignores_approximations(tmp_path):
+    (tmp_path / "solver_config.json").write_text(json.dumps(
+        {"num_inference_steps": 4, "guidance_scale": 3.0, "qaoa_enabled": True, "solver_type": "piecewise_qaoa",
+         "cfg_stride": 2, "unknown_key": 1}))
+    cfg = SolverConfig.from_dir(tmp_path, fallback_model_cfg={"cfg": 7.0, "rescale_t": 3.0})
+    assert cfg.guidance_scale == 3.0 and cfg.solver_type == "piecewise_euler" and cfg.cfg_stride == 1
+    assert "qaoa_enabled" in cfg.approximate_fields_ignored
+
+
+def test_runtime_merge_and_generator_contract():
+    base = FlowMatchSamplingParams(guidance_scale=7.0, num_inference_steps=4)
+    r = resolve(base, FlowMatchSamplingParams(guidance_scale=3.0), cfg_range=[0.4, 1.0])
+    assert r.guidance_scale == 3.0 and r.cfg_range == (0.4, 1.0)
+    with pytest.raises(TypeError):
+        class Bad(LatDitGenerator):  # noqa: F811
+            def generate(self, *a, **k):
+                return None
+
+
+@pytest.mark.parametrize("n", [1, 4095, 4096, 4097, 16384, 70000])
+def test_window_partition_matches_oracle(n):
+    cu, mx = fk.window_seqlens([n], 4096)
+    assert np.array_equal(np.array(cu), geo.window_cu_seqlens(n, 4096))
+    assert mx == min(n, 4096)
+
+
+def test_param_keys_match_oracle_and_checkpoint_names():
+    a = LatDitArch(dim=192, head_dim=96, depth=3, cond_depth=1)
+    o = om.ModelConfig(dim=192, head_dim=96, depth=3, cond_depth=1)
+    assert param_shapes(a) == om.param_shapes(o)
+    full = param_shapes(LatDitArch())
+    assert full["flow.blocks.0.ffn_conv.weight"] == (3, 3, 3, 7680)
+    assert full["flow.blocks.8.cond_gates.weight"] == (3072, 1536)
+    assert full["flow.blocks.0.qk_norm.q_scale"] == (16, 96)
+
+
+def test_arch_rejects_unbuilt_variants():
+    with pytest.raises(NotImplementedError):
+        LatDitArch.from_model_config({"io_conv": True})
+    a = LatDitArch.from_model_config({"dim": 1536, "head_dim": 96})
+    assert a.heads == 16

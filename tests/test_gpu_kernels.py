@@ -1,0 +1,252 @@
+"""GPU parity of each kernel through the C ABI: integer geometry bit-exact
+against the oracle / reference fixtures, floating-point kernels against fp32
+references (tolerances in each test)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from vdit import _lib
+from vdit import fast_kernels as fk
+
+from oracle import geometry as geo
+from oracle import model as om
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def rel(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
+def unique_cells(n, grid, seed):
+    rng = np.random.default_rng(seed)
+    c = rng.choice(grid ** 3, size=n, replace=False)
+    return np.stack([c // (grid * grid), (c // grid) % grid, c % grid], -1).astype(np.int32)
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    yield
+    assert _lib.device_error(clear=True) == 0
+
+
+# ----------------------------------------------------------------------------- geometry (bit-exact)
+
+@pytest.mark.parametrize("case", ["g64", "g128", "shell", "edge"])
+def test_geometry_matches_reference_fixtures(golden, case):
+    vox = torch.from_numpy(golden[f"{case}/vox"]).to(DEV)
+    perm, up, hc = fk.lex_perm(vox)
+    assert np.array_equal(perm.cpu().numpy(), golden[f"{case}/perm"])
+    assert np.array_equal(hc.cpu().numpy(), golden[f"{case}/h_coords"])
+    assert torch.equal(up[perm].cpu(), torch.arange(len(vox)))
+    for bound in (128, 1024):
+        codes, fwd, bwd = fk.hilbert4_orders(hc, bound, return_codes=True)
+        assert np.array_equal(codes.cpu().numpy(), golden[f"{case}/codes4"])
+        assert np.array_equal(fwd.cpu().numpy(), golden[f"{case}/fwd4"])
+        for i in range(4):
+            assert torch.equal(bwd[i][fwd[i]].cpu(), torch.arange(len(vox)))
+    idx = fk.build_conv_indices_fast(hc, already_sorted=True)[0]
+    assert np.array_equal(idx.cpu().numpy(), golden[f"{case}/conv_indices"])
+    raw = torch.cat([torch.zeros(len(vox), 1, dtype=torch.int32, device=DEV), vox], 1)
+    idx2 = fk.build_conv_indices_fast(raw)[0]
+    assert np.array_equal(idx2.cpu().numpy(), golden[f"{case}/conv_indices_unsorted"])
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 5, 127, 4097, 262144])
+def test_geometry_sizes_128grid(n):
+    """C2 geometry: unique uniform voxels in 128^3 (21-bit codes), up to 262144."""
+    vox = unique_cells(n, 128, n)
+    g = geo.sample_geometry(vox)
+    perm, up, hc = fk.lex_perm(torch.from_numpy(vox).to(DEV))
+    assert np.array_equal(perm.cpu().numpy(), g["perm"])
+    codes, fwd, _ = fk.hilbert4_orders(hc, 128, return_codes=True)
+    assert np.array_equal(codes.cpu().numpy(), g["codes4"])
+    assert np.array_equal(fwd.cpu().numpy(), np.stack([f for f, _ in g["order_caches"]]))
+    if n <= 5000:
+        idx = fk.build_conv_indices_fast(hc, already_sorted=True)[0]
+        assert np.array_equal(idx.cpu().numpy(), g["conv_indices"])
+    assert int(codes.max()) < 2 ** 24
+
+
+def test_conv_indices_dense_shell():
+    from tests.golden.make_golden import shell_voxels
+    vox = shell_voxels(16384, 64, 30.0, 7)
+    g = geo.sample_geometry(vox)
+    _, _, hc = fk.lex_perm(torch.from_numpy(vox).to(DEV))
+    idx = fk.build_conv_indices_fast(hc, already_sorted=True)[0].cpu().numpy()
+    assert np.array_equal(idx, g["conv_indices"])
+    assert (idx >= 0).sum(1).mean() > 3     # a surface: several neighbours per voxel
+
+
+@pytest.mark.parametrize("res,hd", [(64, 96), (128, 128)])
+def test_rope_tables(golden, res, hd):
+    c, s = fk.precompute_rope_3d_table(res, 128.0, hd, device=DEV)
+    np.testing.assert_array_max_ulp(c.cpu().numpy(), golden[f"rope3d_{res}_{hd}/cos"], maxulp=1)
+    np.testing.assert_array_max_ulp(s.cpu().numpy(), golden[f"rope3d_{res}_{hd}/sin"], maxulp=1)
+    c2, s2 = fk.precompute_rope_2d_cond(64, 64.0, hd, device=DEV)
+    np.testing.assert_array_max_ulp(c2.cpu().numpy().reshape(-1), golden[f"rope2d_64_{hd}/cos"].reshape(-1), maxulp=1)
+    np.testing.assert_array_max_ulp(s2.cpu().numpy().reshape(-1), golden[f"rope2d_64_{hd}/sin"].reshape(-1), maxulp=1)
+
+
+# ----------------------------------------------------------------------------- row kernels
+
+@pytest.mark.parametrize("m,d", [(1, 1536), (1000, 1536), (333, 192), (4101, 768)])
+def test_modulate_and_gate_add(m, d):
+    g = torch.Generator(device=DEV).manual_seed(m + d)
+    x = torch.randn(m, d, device=DEV, generator=g).to(torch.bfloat16)
+    h = torch.randn(m, d, device=DEV, generator=g).to(torch.bfloat16)
+    s1, sh, gt = [torch.randn(d, device=DEV, generator=g) * 0.3 + o for o in (1.0, 0.0, 0.0)]
+    ref = om.layer_norm(x.float()) * s1 + sh
+    assert rel(fk.fast_modulate(x, None, s1, sh), ref) < 1e-2        # bf16 output rounding
+    x2 = x.clone()
+    mod = fk.fast_gate_add_and_modulate(x2, h, gt, s1, sh)
+    xr = x.float() + h.float() * gt
+    assert rel(x2, xr) < 5e-3
+    assert rel(mod, om.layer_norm(x2.float()) * s1 + sh) < 1e-2
+    x3 = x.clone()
+    fk.fast_gate_add_and_modulate(x3, h[0], gt, None, None, broadcast_h=True)
+    assert rel(x3, x.float() + h[0].float() * gt) < 5e-3
+
+
+def test_out_modulate_unpatchify():
+    g = torch.Generator(device=DEV).manual_seed(3)
+    x = torch.randn(777, 1536, device=DEV, generator=g).to(torch.bfloat16)
+    s1 = 1 + 0.1 * torch.randn(1536, device=DEV, generator=g)
+    sh = 0.1 * torch.randn(1536, device=DEV, generator=g)
+    w = 0.05 * torch.randn(16, 1536, device=DEV, generator=g)
+    out = fk.fast_out_modulate_unpatchify(x, None, s1, sh, w)
+    ref = (om.layer_norm(x.float()) * s1 + sh) @ w.t()
+    assert out.dtype == torch.float32 and rel(out, ref) < 5e-3
+
+
+def test_patchify():
+    g = torch.Generator(device=DEV).manual_seed(4)
+    xt = torch.randn(500, 16, device=DEV, generator=g)
+    w = torch.randn(1536, 16, device=DEV, generator=g) * 0.2
+    assert rel(fk.patchify(xt, w), xt @ w.t()) < 5e-3
+
+
+@pytest.mark.parametrize("heads,hd,res", [(12, 128, 128), (16, 96, 64), (2, 96, 64)])
+def test_qknorm_rope3d_gather(heads, hd, res):
+    n = 3000
+    vox = unique_cells(n, res, hd)
+    _, _, hc = fk.lex_perm(torch.from_numpy(vox).to(DEV))
+    g = torch.Generator(device=DEV).manual_seed(heads)
+    D = heads * hd
+    qkv = torch.randn(n, 3 * D, device=DEV, generator=g).to(torch.bfloat16)
+    qs = 1 + 0.1 * torch.randn(heads, hd, device=DEV, generator=g)
+    ks = 1 + 0.1 * torch.randn(heads, hd, device=DEV, generator=g)
+    fwd = torch.randperm(n, device=DEV)
+    cos, sin = fk.precompute_rope_3d_table(res, 128.0, hd, device=DEV)
+    out = fk.fused_qknorm_rope3d_gather(qkv, qs, ks, cos, sin, hc, fwd, heads, hd).view(n, 3, heads, hd)
+    src = qkv.float()[fwd].view(n, 3, heads, hd).cpu()
+    pos = ((hc.float()[fwd][:, 1:] + 0.5) / res * 2 - 1).cpu()
+    q = om.rope_nd(om.rms_norm(src[:, 0]) * qs.cpu(), pos, 128.0)
+    k = om.rope_nd(om.rms_norm(src[:, 1]) * ks.cpu(), pos, 128.0)
+    assert rel(out[:, 0], q) < 1e-2 and rel(out[:, 1], k) < 1e-2
+    assert torch.equal(out[:, 2], qkv.view(n, 3, heads, hd)[fwd][:, 2])
+
+
+@pytest.mark.parametrize("heads,hd", [(12, 128), (16, 96)])
+def test_qknorm_rope2d(heads, hd):
+    L = 4101
+    g = torch.Generator(device=DEV).manual_seed(hd)
+    D = heads * hd
+    qkv = torch.randn(L, 3 * D, device=DEV, generator=g).to(torch.bfloat16)
+    ref_in = qkv.float().view(L, 3, heads, hd).cpu()
+    qs = 1 + 0.1 * torch.randn(heads, hd, device=DEV, generator=g)
+    ks = 1 + 0.1 * torch.randn(heads, hd, device=DEV, generator=g)
+    cos, sin = fk.precompute_rope_2d_cond(64, 64.0, hd, device=DEV)
+    fk.fused_qknorm_rope2d_cond_inplace(qkv, qs, ks, cos, sin, heads, hd)
+    out = qkv.view(L, 3, heads, hd)
+    cpos = om.cond_positions(L)
+    q = om.rms_norm(ref_in[:, 0]) * qs.cpu()
+    k = om.rms_norm(ref_in[:, 1]) * ks.cpu()
+    q = torch.cat([q[:5], om.rope_nd(q[5:], cpos, 64.0)])
+    k = torch.cat([k[:5], om.rope_nd(k[5:], cpos, 64.0)])
+    assert rel(out[:, 0], q) < 1e-2 and rel(out[:, 1], k) < 1e-2
+    assert torch.equal(out[:, 2].float().cpu(), ref_in[:, 2])
+
+
+def test_swiglu():
+    g = torch.Generator(device=DEV).manual_seed(9)
+    h = torch.randn(4101, 7680, device=DEV, generator=g).to(torch.bfloat16)
+    a, gg = h.float().chunk(2, -1)
+    assert rel(fk.fast_swiglu_from_packed(h), torch.nn.functional.silu(gg) * a) < 1e-2
+
+
+@pytest.mark.parametrize("c", [7680, 960])
+def test_dwconv27(c):
+    from tests.golden.make_golden import shell_voxels
+    vox = shell_voxels(6000, 64, 24.0, 11)
+    _, _, hc = fk.lex_perm(torch.from_numpy(vox).to(DEV))
+    idx = fk.build_conv_indices_fast(hc, already_sorted=True)[0]
+    g = torch.Generator(device=DEV).manual_seed(c)
+    n = len(vox)
+    h = torch.randn(n, c, device=DEV, generator=g).to(torch.bfloat16)
+    w = 0.2 * torch.randn(27, c, device=DEV, generator=g)
+    b = 0.1 * torch.randn(c, device=DEV, generator=g)
+    ref = om.dwconv27(h.float().cpu(), w.cpu(), b.cpu(), idx.cpu())
+    assert rel(fk.fast_sparse_conv3d(h, w, b, [idx]), ref) < 1e-2
+    a, gg = ref.chunk(2, -1)
+    assert rel(fk.fast_sparse_conv3d(h, w, b, [idx], fuse_swiglu=True), torch.nn.functional.silu(gg) * a) < 1e-2
+
+
+# ----------------------------------------------------------------------------- attention
+
+def ref_attention(q, k, v, cu_q, cu_k, heads, hd):
+    out = torch.empty(q.shape[0], heads, hd, device=q.device)
+    qf, kf, vf = (t.float().reshape(t.shape[0], heads, hd) for t in (q, k, v))
+    for i in range(len(cu_q) - 1):
+        a, b, c, d = cu_q[i], cu_q[i + 1], cu_k[i], cu_k[i + 1]
+        if b > a:
+            out[a:b] = torch.nn.functional.scaled_dot_product_attention(
+                qf[a:b].transpose(0, 1), kf[c:d].transpose(0, 1), vf[c:d].transpose(0, 1)).transpose(0, 1)
+    return out.reshape(q.shape[0], heads * hd)
+
+
+@pytest.mark.parametrize("heads,hd", [(12, 128), (16, 96)])
+@pytest.mark.parametrize("cu_q,cu_k", [
+    ([0, 4096, 5000], [0, 4096, 5000]),          # windows, ragged tail
+    ([0, 1000], [0, 4101]),                      # voxel -> context
+    ([0, 4101], [0, 1000]),                      # context -> voxel
+    ([0, 1], [0, 1]), ([0, 130], [0, 3]), ([0, 7, 300, 301], [0, 129, 130, 700]),
+])
+def test_attention_matches_fp32(heads, hd, cu_q, cu_k):
+    g = torch.Generator(device=DEV).manual_seed(len(cu_q) * 7 + cu_q[-1] + hd)
+    D = heads * hd
+    nq, nk = cu_q[-1], cu_k[-1]
+    q = torch.randn(nq, D, device=DEV, generator=g).to(torch.bfloat16)
+    kv = torch.randn(nk, 2 * D, device=DEV, generator=g).to(torch.bfloat16)   # packed, strided views
+    out = fk.attention(q, kv[:, :D], kv[:, D:], cu_q, cu_k, heads, hd)
+    ref = ref_attention(q, kv[:, :D], kv[:, D:], cu_q, cu_k, heads, hd)
+    assert rel(out, ref) < 1e-2
+
+
+def test_attention_scatter_and_large_logits():
+    heads, hd, n = 12, 128, 4096 + 700
+    g = torch.Generator(device=DEV).manual_seed(1)
+    qkv = torch.randn(n, 3 * heads * hd, device=DEV, generator=g)
+    qkv[:, : heads * hd] *= 6.0          # peaky softmax: exercises the deferred O rescale
+    qkv = qkv.to(torch.bfloat16)
+    D = heads * hd
+    rows = torch.randperm(n, device=DEV)
+    out = fk.flash_varlen_qkvpacked_already_sorted(qkv, torch.tensor([0, 4096, n]), 4096, heads, hd,
+                                                   out_rows=rows)
+    ref = ref_attention(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], [0, 4096, n], [0, 4096, n], heads, hd)
+    assert rel(out[rows], ref) < 1e-2
+
+
+@pytest.mark.parametrize("n,heads,hd", [(1, 12, 128), (1000, 12, 128), (16384, 12, 128), (5000, 16, 96)])
+def test_attention_1q(n, heads, hd):
+    g = torch.Generator(device=DEV).manual_seed(n)
+    D = heads * hd
+    q = torch.randn(D, device=DEV, generator=g)
+    kv = torch.randn(n, 2 * D, device=DEV, generator=g).to(torch.bfloat16)
+    out = fk.attention_1q(q, kv, heads, hd)
+    ref = ref_attention(q.to(torch.bfloat16)[None], kv[:, :D], kv[:, D:], [0, 1], [0, n], heads, hd)[0]
+    assert rel(out, ref) < 1e-2
