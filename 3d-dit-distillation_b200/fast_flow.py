@@ -350,7 +350,15 @@ class OptimizedLatDitRunner:
         """Exact Euler + CFG sampler; returns [N,16] fp32 latents in the input voxel order.
         ``noise`` ([N,16], input order) overrides the generator draw."""
         context = self.encode_context(conditioning.dino_features)
-        geom = self._prepare_sample_geometry(vox_idxs, context)
+        return [self.sample_with_context(vox_idxs[0], context, sampling=sampling, generator=generator, noise=noise)]
+
+    @torch.no_grad()
+    def sample_with_context(self, vox: torch.Tensor, context: torch.Tensor, *,
+                            sampling: Optional[FlowMatchSamplingParams] = None,
+                            generator: Optional[torch.Generator] = None,
+                            noise: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """The sampler on one sample with the image context already mapped ([L, D])."""
+        geom = self._prepare_sample_geometry([vox], context)
         N = geom["N"]
         if noise is None:
             noise = torch.randn(N, self.latent_dim, dtype=F32, device=self.device, generator=generator)
@@ -372,8 +380,7 @@ class OptimizedLatDitRunner:
                 vn = self.forward_flow_fast(xt, tl[i], context, None, geom, uncond=True)
             fk.cfg_euler_(xt, v, vn, g_scale, tl[i] - tl[i + 1])
         self._b0_share = None
-        out = fk.unpermute_denorm(xt, geom["up_widx"], self._denorm_scale, self._denorm_shift)
-        return [out]
+        return fk.unpermute_denorm(xt, geom["up_widx"], self._denorm_scale, self._denorm_shift)
 
     @torch.no_grad()
     def warmup(self) -> None:
