@@ -1,19 +1,23 @@
 // Non-causal varlen flash attention on Blackwell tensor cores (tcgen05 + TMEM + TMA).
 //
-// One CTA computes a 128-query tile of one head of one segment.  Warp roles:
-//   warp 0      TMA producer: Q once, then K/V tiles (128 keys) into a 2-stage ring
-//   warp 1      MMA issuer (one elected thread): S = Q K^T into a double-buffered
-//               TMEM accumulator, O += P V into a TMEM accumulator
-//   warps 2..5  softmax group: one query row per thread; reads S from TMEM,
-//               online softmax in fp32 (exp2), writes P (bf16) to shared memory,
-//               rescales O in TMEM only when the running max grew by more than
-//               2^8 (exact: the final O/l uses the same reference max), and runs
-//               the epilogue (O / l -> bf16 -> global, optional row scatter).
+// One CTA computes two 128-query tiles (256 rows) of one head of one segment.
+// Warp roles:
+//   warp 0      TMA producer: Q (both tiles) once, then K/V tiles of 128 keys into
+//               a 2-stage ring
+//   warp 1      MMA issuer (one elected thread): S_g = Q_g K^T into TMEM, then
+//               O_g += P_g V with P_g read from TMEM (the A operand in tensor memory)
+//   warps 2..5  softmax warpgroup of tile 0, warps 6..9 of tile 1: one query row
+//               per thread; row max from TMEM, P = exp2(S*scale - m) in fp32 written
+//               back to TMEM as bf16 over the S columns, O rescaled in TMEM only when
+//               the running max grew by more than 2^8 (exact: the final O/l uses the
+//               same reference max); then the epilogue O / l -> bf16 -> global with
+//               an optional row scatter.
+// While one tile's softmax runs, the tensor core works on the other tile.
 // Shared-memory operands use the canonical UMMA layouts: Q/K K-major with 64-byte
-// swizzle (TMA boxes of 32 channels), V MN-major with 64-byte swizzle, P K-major
-// with 128-byte swizzle.  No cluster multicast is used anywhere.
-// Every mbarrier wait is bounded; a wait that runs out records an error in
-// g_device_error, raises a CTA abort flag and the CTA skips to its teardown.
+// swizzle (TMA boxes of 32 channels), V MN-major with 64-byte swizzle.  No cluster
+// multicast is used anywhere.  Every mbarrier wait is bounded; a wait that runs
+// out records an error in g_device_error, raises a CTA abort flag and the CTA
+// skips to its teardown (TMEM is always freed).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -32,7 +36,7 @@ namespace fmha {
 constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int STAGES = 2;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;   // TMA warp, MMA warp, 2 softmax warpgroups
 constexpr int MAXSEG = 128;
 constexpr uint32_t kSpinLimit = 1u << 22;   // try_wait polls before a wait is declared stuck
 constexpr int kErrTimeout = 0x4154;   // "AT"
@@ -147,6 +151,46 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+
+// D (TMEM) += A (TMEM) * B (smem descriptor)
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns from 16 registers per thread
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+// packed fp32x2 FMA: (a.x*s + b, a.y*s + b)
+__device__ __forceinline__ float2 ffma2(float2 a, float s, float b) {
+    unsigned long long ra, rs, rb, rd;
+    asm("mov.b64 %0, {%1,%2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
+    asm("mov.b64 %0, {%1,%1};" : "=l"(rs) : "f"(s));
+    asm("mov.b64 %0, {%1,%1};" : "=l"(rb) : "f"(b));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(rd) : "l"(ra), "l"(rs), "l"(rb));
+    float2 o;
+    asm("mov.b64 {%0,%1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(rd));
+    return o;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float m;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
+    return m;
+}
+
 // Shared-memory matrix descriptors (sm_100 format: start>>4 in [0,14), LBO>>4 in
 // [16,30), SBO>>4 in [32,46), version 1 at bit 46, layout type in [61,64)).
 __device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint64_t layout) {
@@ -162,6 +206,15 @@ __host__ __device__ constexpr uint32_t make_idesc(int m, int n, bool b_mn_major)
 }
 
 // ---------------------------------------------------------------- kernel
+// Two 128-row query tiles per CTA (rows q_row0 .. q_row0+255), each with its
+// own softmax warpgroup, S/P and O accumulators in TMEM:
+//   tile g: S_g (fp32, 128 cols) at col 256g, overwritten in place by P_g
+//           (bf16 pairs, 64 cols) once read; O_g at col 256g + 128.
+// MMA issue order per key tile j: PV0(j), S0(j+1), PV1(j), S1(j+1), so the
+// tensor core computes one tile's products while the other tile's softmax
+// runs.  tcgen05 MMAs of one thread execute in issue order, and a commit
+// tracks every earlier MMA of that thread, so "S_g(j+1) complete" also means
+// "PV_g(j) complete": the softmax group may then rescale O_g and overwrite P_g.
 template <int HD>
 __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                               const __grid_constant__ CUtensorMap tmK,
@@ -172,35 +225,33 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
     constexpr int NCH = HD / 32;                 // 64-byte channel chunks per row
     constexpr int CHUNK = BM * 64;               // bytes of one chunk of a 128-row tile
     constexpr int TILE = NCH * CHUNK;            // bytes of one 128-row Q/K/V tile
-    constexpr int PBYTES = BM * BN * 2;
     constexpr uint32_t IDESC_QK = make_idesc(BM, BN, false);
     constexpr uint32_t IDESC_PV = make_idesc(BM, HD, true);
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = smem;
-    uint8_t* sK = sQ + TILE;
-    uint8_t* sV = sK + STAGES * TILE;
-    uint8_t* sP = sV + STAGES * TILE;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + PBYTES);
+    uint8_t* sQ = smem;                          // [2 tiles]
+    uint8_t* sK = sQ + 2 * TILE;                 // [STAGES]
+    uint8_t* sV = sK + STAGES * TILE;            // [STAGES]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + STAGES * TILE);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const uint32_t b_q = smem_u32(&bars[0]);
     auto b_kvfull = [&](int s) { return smem_u32(&bars[1 + s]); };
     auto b_kvempty = [&](int s) { return smem_u32(&bars[3 + s]); };
-    auto b_sfull = [&](int s) { return smem_u32(&bars[5 + s]); };
-    auto b_sempty = [&](int s) { return smem_u32(&bars[7 + s]); };
-    const uint32_t b_pfull = smem_u32(&bars[9]);
-    const uint32_t b_pvdone = smem_u32(&bars[10]);
+    auto b_sfull = [&](int g) { return smem_u32(&bars[5 + g]); };
+    auto b_pfull = [&](int g) { return smem_u32(&bars[7 + g]); };
+    auto b_odone = [&](int g) { return smem_u32(&bars[9 + g]); };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int head = blockIdx.y;
-    const int tile = blockIdx.x;
+    const int pair = blockIdx.x;
     int s = 0;
-    while (s + 1 < seg.nseg && seg.tile0[s + 1] <= tile) ++s;
-    const int q_row0 = seg.q0[s] + (tile - seg.tile0[s]) * BM;
-    const int q_rows = min(BM, seg.q0[s + 1] - q_row0);
+    while (s + 1 < seg.nseg && seg.tile0[s + 1] <= pair) ++s;
+    const int q_row0 = seg.q0[s] + (pair - seg.tile0[s]) * (2 * BM);
+    const int q_rows = min(2 * BM, seg.q0[s + 1] - q_row0);
+    const bool has1 = q_rows > BM;                       // CTA-uniform
     const int k_begin = seg.k0[s];
     const int k_len = seg.k0[s + 1] - k_begin;
     const int n_kv = (k_len + BN - 1) / BN;
@@ -215,14 +266,13 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
 
     if (threadIdx.x == 0) {
         mbar_init(b_q, 1);
-        for (int i = 0; i < STAGES; ++i) {
+        for (int i = 0; i < 2; ++i) {
             mbar_init(b_kvfull(i), 1);
             mbar_init(b_kvempty(i), 1);
             mbar_init(b_sfull(i), 1);
-            mbar_init(b_sempty(i), 128);
+            mbar_init(b_pfull(i), 128);
+            mbar_init(b_odone(i), 1);
         }
-        mbar_init(b_pfull, 128);
-        mbar_init(b_pvdone, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmQ)) : "memory");
@@ -237,13 +287,14 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tmem_O = tmem + 2 * BN;
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
-            mbar_expect_tx(b_q, TILE);
-            for (int c = 0; c < NCH; ++c) tma_load_3d(smem_u32(sQ + c * CHUNK), &tmQ, c * 32, head, q_row0, b_q);
+            mbar_expect_tx(b_q, (has1 ? 2 : 1) * TILE);
+            for (int t = 0; t < (has1 ? 2 : 1); ++t)
+                for (int c = 0; c < NCH; ++c)
+                    tma_load_3d(smem_u32(sQ + t * TILE + c * CHUNK), &tmQ, c * 32, head, q_row0 + t * BM, b_q);
             for (int j = 0; j < n_kv; ++j) {
                 const int st = j & 1;
                 if (j >= STAGES && !mbar_wait(b_kvempty(st), ((j - STAGES) >> 1) & 1, abort_flag)) break;
@@ -258,131 +309,148 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            bool ok = mbar_wait(b_q, 0, abort_flag);
-            auto issue_pv = [&](int t) -> bool {
-                if (!mbar_wait(b_pfull, t & 1, abort_flag)) return false;
-                tc_fence_after();
-                const int stv = t & 1;
-                const uint32_t pbase = smem_u32(sP), vbase = smem_u32(sV + stv * TILE);
-#pragma unroll
-                for (int kk = 0; kk < BN / 16; ++kk) {
-                    const uint64_t a = make_desc(pbase + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024, kSw128);
-                    const uint64_t b = make_desc(vbase + kk * 16 * 64, CHUNK, 512, kSw64);
-                    tc_mma(tmem_O, a, b, IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
-                }
-                tc_commit(b_pvdone);
-                tc_commit(b_kvempty(stv));
-                return true;
-            };
-            for (int j = 0; ok && j < n_kv; ++j) {
-                const int st = j & 1;
-                if (!mbar_wait(b_kvfull(st), (j >> 1) & 1, abort_flag)) { ok = false; break; }
-                if (j >= 2 && !mbar_wait(b_sempty(st), ((j - 2) >> 1) & 1, abort_flag)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t qbase = smem_u32(sQ), kbase = smem_u32(sK + st * TILE);
+            const int ntile = has1 ? 2 : 1;
+            auto issue_s = [&](int g, int j) {
+                const uint32_t qbase = smem_u32(sQ + g * TILE), kbase = smem_u32(sK + (j & 1) * TILE);
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk) {
                     const uint32_t off = (kk >> 1) * CHUNK + (kk & 1) * 32;
-                    const uint64_t a = make_desc(qbase + off, 16, 512, kSw64);
-                    const uint64_t b = make_desc(kbase + off, 16, 512, kSw64);
-                    tc_mma(tmem + st * BN, a, b, IDESC_QK, kk > 0 ? 1u : 0u);
+                    tc_mma(tmem + g * 256, make_desc(qbase + off, 16, 512, kSw64),
+                           make_desc(kbase + off, 16, 512, kSw64), IDESC_QK, kk > 0 ? 1u : 0u);
                 }
-                tc_commit(b_sfull(st));
-                if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+            };
+            auto issue_pv = [&](int g, int j) {
+                const uint32_t vbase = smem_u32(sV + (j & 1) * TILE);
+#pragma unroll
+                for (int kk = 0; kk < BN / 16; ++kk) {
+                    tc_mma_ts(tmem + g * 256 + 128, tmem + g * 256 + kk * 8, make_desc(vbase + kk * 16 * 64, CHUNK, 512,
+                              kSw64), IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+                }
+            };
+            bool ok = mbar_wait(b_q, 0, abort_flag) && mbar_wait(b_kvfull(0), 0, abort_flag);
+            if (ok) {
+                tc_fence_after();
+                for (int g = 0; g < ntile; ++g) {
+                    issue_s(g, 0);
+                    tc_commit(b_sfull(g));
+                }
             }
-            if (ok) issue_pv(n_kv - 1);
+            for (int j = 0; ok && j < n_kv; ++j) {
+                const bool more = j + 1 < n_kv;
+                for (int g = 0; g < ntile; ++g) {
+                    if (!mbar_wait(b_pfull(g), j & 1, abort_flag)) { ok = false; break; }
+                    if (g == 0 && more && !mbar_wait(b_kvfull((j + 1) & 1), ((j + 1) >> 1) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_pv(g, j);
+                    if (more) {
+                        issue_s(g, j + 1);
+                        tc_commit(b_sfull(g));
+                    } else {
+                        tc_commit(b_odone(g));
+                    }
+                }
+                if (ok) tc_commit(b_kvempty(j & 1));
+            }
         }
     } else {
-        // ------------------------------------------------------------ softmax group
+        // ------------------------------------------------------------ softmax groups
+        const int g = (warp - 2) >> 2;                   // query tile of this warpgroup
         const int quarter = warp & 3;                    // TMEM lane quarter this warp may access
-        const int row = quarter * 32 + lane;
+        const int row = quarter * 32 + lane;             // row inside the tile
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-        float m_run = -INFINITY, l_run = 0.f;
-        bool ok = true;
-        uint8_t* prow = sP + row * 128;
-        for (int j = 0; j < n_kv; ++j) {
-            const int st = j & 1;
-            // every lane runs each wait, then the warp agrees, so an abort never splits the warp
-            ok = __all_sync(0xffffffffu, mbar_wait(b_sfull(st), (j >> 1) & 1, abort_flag));
-            if (!ok) break;
-            tc_fence_after();
-            float sv[BN];
-#pragma unroll
-            for (int c = 0; c < BN / 32; ++c) tmem_ld32(tmem + lane_off + st * BN + c * 32, sv + c * 32);
-            tmem_wait_ld();
-            tc_fence_before();
-            mbar_arrive(b_sempty(st));
-            const int valid = min(BN, k_len - j * BN);
-            float mt = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < BN; ++c) {
-                if (c >= valid) sv[c] = -INFINITY;
-                mt = fmaxf(mt, sv[c]);
-            }
-            const float m_new = fmaxf(m_run, mt * scale_log2);
-            if (j > 0) {
-                ok = __all_sync(0xffffffffu, mbar_wait(b_pvdone, (j - 1) & 1, abort_flag));
+        const uint32_t tS = tmem + g * 256 + lane_off, tO = tS + 128;
+        if (g == 0 || has1) {
+            float m_run = -INFINITY, l_run = 0.f;
+            bool ok = true;
+            for (int j = 0; j < n_kv; ++j) {
+                // every lane runs each wait, then the warp agrees, so an abort never splits the warp
+                ok = __all_sync(0xffffffffu, mbar_wait(b_sfull(g), j & 1, abort_flag));
                 if (!ok) break;
                 tc_fence_after();
+                const int valid = min(BN, k_len - j * BN);
+                float mt = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < BN / 32; ++c) {
+                    float v[32];
+                    tmem_ld32(tS + c * 32, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2) {
+                        const float a = (c * 32 + i < valid) ? v[i] : -INFINITY;
+                        const float b2 = (c * 32 + i + 1 < valid) ? v[i + 1] : -INFINITY;
+                        mt = fmax3(mt, a, b2);
+                    }
+                }
+                const float m_new = fmaxf(m_run, mt * scale_log2);
+                float alpha = 1.f;
+                bool rescale = false;
+                if (j == 0) {
+                    m_run = m_new;
+                } else if (m_new > m_run + 8.f) {
+                    alpha = ex2(m_run - m_new);
+                    m_run = m_new;
+                    l_run *= alpha;
+                    rescale = true;
+                }
+                if (__any_sync(0xffffffffu, rescale)) {      // warp-uniform TMEM round trip
+#pragma unroll 1
+                    for (int c = 0; c < HD / 32; ++c) {
+                        float ov[32];
+                        tmem_ld32(tO + c * 32, ov);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+                        tmem_st32(tO + c * 32, ov);
+                    }
+                }
+                // P = exp2(S*scale - m) as bf16 pairs, written over the S columns already read
+                float lsum = 0.f;
+                const float nm = -m_run;
+#pragma unroll
+                for (int c = 0; c < BN / 32; ++c) {
+                    float v[32];
+                    tmem_ld32(tS + c * 32, v);
+                    tmem_wait_ld();
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2) {
+                        float2 e = ffma2(make_float2(v[i], v[i + 1]), scale_log2, nm);
+                        float p0 = (c * 32 + i < valid) ? ex2(e.x) : 0.f;
+                        float p1 = (c * 32 + i + 1 < valid) ? ex2(e.y) : 0.f;
+                        lsum += p0 + p1;
+                        __nv_bfloat162 bp = __floats2bfloat162_rn(p0, p1);
+                        pk[i >> 1] = *reinterpret_cast<uint32_t*>(&bp);
+                    }
+                    tmem_st16(tS + c * 16, pk);
+                }
+                l_run += lsum;
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(b_pfull(g));
             }
-            float alpha = 1.f;
-            bool rescale = false;
-            if (j == 0) {
-                m_run = m_new;
-            } else if (m_new > m_run + 8.f) {
-                alpha = ex2(m_run - m_new);
-                m_run = m_new;
-                l_run *= alpha;
-                rescale = true;
-            }
-            if (__any_sync(0xffffffffu, rescale)) {      // warp-uniform TMEM round trip
+            // -------------------------------------------------------- epilogue
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(b_odone(g), 0, abort_flag));
+            if (ok) {
+                tc_fence_after();
+                const float inv = 1.f / l_run;
+                const int qr = g * BM + row;
+                const bool live = qr < q_rows;
+                const int64_t orow = live ? (out_rows ? out_rows[q_row0 + qr] : (int64_t)(q_row0 + qr)) : 0;
+                __nv_bfloat16* dst = out + orow * out_stride + (int64_t)head * HD;
 #pragma unroll 1
                 for (int c = 0; c < HD / 32; ++c) {
                     float ov[32];
-                    tmem_ld32(tmem_O + lane_off + c * 32, ov);
+                    tmem_ld32(tO + c * 32, ov);
                     tmem_wait_ld();
+                    if (live) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-                    tmem_st32(tmem_O + lane_off + c * 32, ov);
-                }
-                tmem_wait_st();
-            }
-            // P = exp2(S*scale - m) as bf16 into the 128B-swizzled K-major tile
-            float lsum = 0.f;
+                        for (int i = 0; i < 32; ++i) ov[i] *= inv;
 #pragma unroll
-            for (int q = 0; q < BN / 8; ++q) {
-                float p[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    p[i] = ex2(fmaf(sv[q * 8 + i], scale_log2, -m_run));
-                    lsum += p[i];
-                }
-                const int region = q >> 3, lc = q & 7;
-                *reinterpret_cast<uint4*>(prow + region * (BM * 128) + ((lc ^ (row & 7)) << 4)) = pack8(p);
-            }
-            l_run += lsum;
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            tc_fence_before();
-            mbar_arrive(b_pfull);
-        }
-        // ------------------------------------------------------------ epilogue
-        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(b_pvdone, (n_kv - 1) & 1, abort_flag));
-        if (ok) {
-            tc_fence_after();
-            const float inv = 1.f / l_run;
-            const bool live = row < q_rows;
-            const int64_t orow = live ? (out_rows ? out_rows[q_row0 + row] : (int64_t)(q_row0 + row)) : 0;
-            __nv_bfloat16* dst = out + orow * out_stride + (int64_t)head * HD;
-#pragma unroll 1
-            for (int c = 0; c < HD / 32; ++c) {
-                float ov[32];
-                tmem_ld32(tmem_O + lane_off + c * 32, ov);
-                tmem_wait_ld();
-                if (live) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) ov[i] *= inv;
-#pragma unroll
-                    for (int v = 0; v < 4; ++v) *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) = pack8(ov + v * 8);
+                        for (int v = 0; v < 4; ++v) *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) = pack8(ov + v * 8);
+                    }
                 }
             }
         }
@@ -425,7 +493,7 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int heads, int hd,
 
 template <int HD>
 size_t smem_bytes() {
-    return 1024 + (size_t)HD * 256 * (1 + 2 * STAGES) + (size_t)BM * BN * 2 + 128;
+    return 1024 + (size_t)HD * 256 * (2 + 2 * STAGES) + 128;
 }
 
 template <int HD>
@@ -471,7 +539,7 @@ extern "C" int vdit_attention(const void* q, int64_t q_stride, const void* k, in
         seg.q0[i] = cu_q[i];
         seg.k0[i] = cu_k[i];
         seg.tile0[i] = tiles;
-        if (i < nseg) tiles += (cu_q[i + 1] - cu_q[i] + BM - 1) / BM;
+        if (i < nseg) tiles += (cu_q[i + 1] - cu_q[i] + 2 * BM - 1) / (2 * BM);   // 256-row tile pairs
     }
     if (tiles == 0) return VDIT_OK;
     const int64_t q_rows = cu_q[nseg], k_rows = cu_k[nseg];

@@ -161,78 +161,92 @@ __global__ void __launch_bounds__(256) out_unpatchify_kernel(const __nv_bfloat16
 }
 
 // ---------------------------------------------------------------- QK norm + RoPE
-// One block per token row; the row (3*heads*hd bf16) is staged in shared
-// memory, each warp normalises and rotates whole head vectors, and the block
-// writes the finished row back with 16-byte stores.
+// One warp per (token row, head): lanes 0..15 hold the head's q vector, lanes
+// 16..31 its k vector (8 channels each, one 16-byte load per lane; head_dim 96
+// uses 12 lanes per half).  RMS statistics reduce over the 16-lane half with
+// shuffles; the normalised values go through a per-warp shared-memory slot so
+// each lane can read its RoPE partner channel (e +- M); v is copied through.
 //   MODE 0: 3D RoPE, positions from h_coords[src] via the [res, hd/6] tables,
 //           optional gather src = fwd[dst].
 //   MODE 1: 2D RoPE on tokens >= n_prefix via [L-n_prefix, 2, hd/4] tables, in place.
+constexpr int kQkWarps = 8;
+
 template <int MODE>
-__global__ void __launch_bounds__(128) qknorm_rope_kernel(
+__global__ void __launch_bounds__(kQkWarps * 32) qknorm_rope_kernel(
     const __nv_bfloat16* __restrict__ in, __nv_bfloat16* __restrict__ out, int64_t rows, int heads, int hd,
     const float* __restrict__ qs, const float* __restrict__ ks, const float* __restrict__ cs,
     const float* __restrict__ sn, int res, const int4* __restrict__ hc, const int64_t* __restrict__ fwd,
     int n_prefix) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int D = heads * hd;
-    __nv_bfloat16* srow = reinterpret_cast<__nv_bfloat16*>(smem_raw);
-    float* snorm = reinterpret_cast<float*>(smem_raw + ((3 * D * 2 + 15) & ~15));   // [4 warps][hd]
-    const int64_t dst = blockIdx.x;
-    const int64_t src = (MODE == 0 && fwd != nullptr) ? fwd[dst] : dst;
-    const int nvec = 3 * D / 8;
-    const __nv_bfloat16* irow = in + src * (int64_t)(3 * D);
-    for (int v = threadIdx.x; v < nvec; v += blockDim.x)
-        reinterpret_cast<uint4*>(srow)[v] = reinterpret_cast<const uint4*>(irow)[v];
-    __syncthreads();
-
+    __shared__ float snorm[kQkWarps][2][128];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int coord[3] = {0, 0, 0};
-    bool rotate = true;
-    int ptok = 0;
-    if (MODE == 0) {
-        int4 c = hc[src];
-        coord[0] = min(max(c.y, 0), res - 1);
-        coord[1] = min(max(c.z, 0), res - 1);
-        coord[2] = min(max(c.w, 0), res - 1);
-    } else {
-        rotate = dst >= n_prefix;
-        ptok = (int)(dst - n_prefix);
+    const int64_t item = (int64_t)blockIdx.x * kQkWarps + warp;
+    if (item >= rows * heads) return;
+    const int64_t dst = item / heads;
+    const int h = (int)(item % heads);
+    const int64_t src = (MODE == 0 && fwd != nullptr) ? fwd[dst] : dst;
+    const int D = heads * hd;
+    const int half = lane >> 4, vi = lane & 15;                 // half 0 = q, 1 = k
+    const bool active = vi * 8 < hd;
+    const __nv_bfloat16* irow = in + src * (int64_t)(3 * D) + (int64_t)h * hd;
+    __nv_bfloat16* orow = out + dst * (int64_t)(3 * D) + (int64_t)h * hd;
+
+    float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    uint4 vcopy = make_uint4(0, 0, 0, 0);
+    if (active) {
+        load8(irow + half * D + vi * 8, x);
+        if (half == 0) vcopy = *reinterpret_cast<const uint4*>(irow + 2 * D + vi * 8);
     }
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss += x[j] * x[j];
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rr = rsqrtf(ss / (float)hd + 1e-6f);
+    const float* scale = (half == 0 ? qs : ks) + h * hd;
+    float* nb = snorm[warp][half];
+    if (active) {
+        const float4 s0 = __ldg(reinterpret_cast<const float4*>(scale + vi * 8));
+        const float4 s1 = __ldg(reinterpret_cast<const float4*>(scale + vi * 8 + 4));
+        const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            x[j] = bf2f(f2bf(x[j] * rr)) * sc[j];            // normalised value rounded like the reference
+            nb[vi * 8 + j] = x[j];
+        }
+    }
+    __syncwarp();
+
     const int naxes = MODE == 0 ? 3 : 2;
     const int M = hd / (2 * naxes);
-    float* nb = snorm + warp * hd;
-    for (int hv = warp; hv < 2 * heads; hv += 4) {
-        const int which = hv / heads, h = hv % heads;      // 0 = q, 1 = k
-        __nv_bfloat16* vec = srow + which * D + h * hd;
-        const float* scale = (which == 0 ? qs : ks) + h * hd;
-        float ss = 0.f;
-        for (int e = lane; e < hd; e += 32) { float t = bf2f(vec[e]); ss += t * t; }
-        float rr = rsqrtf(warp_sum(ss) / (float)hd + 1e-6f);
-        for (int e = lane; e < hd; e += 32) nb[e] = bf2f(f2bf(bf2f(vec[e]) * rr)) * __ldg(scale + e);
-        __syncwarp();
-        for (int e = lane; e < hd; e += 32) {
-            float o = nb[e];
-            const int grp = e / (2 * M), off = e % (2 * M);
+    bool rotate = true;
+    int64_t tab_row[3] = {0, 0, 0};
+    if (MODE == 0) {
+        const int4 c = hc[src];
+        tab_row[0] = min(max(c.y, 0), res - 1);
+        tab_row[1] = min(max(c.z, 0), res - 1);
+        tab_row[2] = min(max(c.w, 0), res - 1);
+    } else {
+        rotate = dst >= n_prefix;
+        const int64_t pt = dst - n_prefix;
+        tab_row[0] = pt * 2;
+        tab_row[1] = pt * 2 + 1;
+    }
+    if (active) {
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = vi * 8 + j;
+            const int grp = e / (2 * M), off = e - grp * 2 * M;
+            o[j] = x[j];
             if (rotate && grp < naxes) {
                 const int f = off < M ? off : off - M;
-                float c, s;
-                if (MODE == 0) {
-                    c = __ldg(cs + coord[grp] * M + f);
-                    s = __ldg(sn + coord[grp] * M + f);
-                } else {
-                    c = __ldg(cs + ((int64_t)ptok * 2 + grp) * M + f);
-                    s = __ldg(sn + ((int64_t)ptok * 2 + grp) * M + f);
-                }
-                o = off < M ? nb[e] * c - nb[e + M] * s : nb[e] * c + nb[e - M] * s;
+                const float c = __ldg(cs + tab_row[grp] * M + f), s = __ldg(sn + tab_row[grp] * M + f);
+                o[j] = off < M ? x[j] * c - nb[e + M] * s : x[j] * c + nb[e - M] * s;
             }
-            vec[e] = f2bf(o);
         }
-        __syncwarp();
+        store8(orow + half * D + vi * 8, o);
+        if (half == 0) *reinterpret_cast<uint4*>(orow + 2 * D + vi * 8) = vcopy;
     }
-    __syncthreads();
-    __nv_bfloat16* orow = out + dst * (int64_t)(3 * D);
-    for (int v = threadIdx.x; v < nvec; v += blockDim.x)
-        reinterpret_cast<uint4*>(orow)[v] = reinterpret_cast<const uint4*>(srow)[v];
 }
 
 // ---------------------------------------------------------------- misc
@@ -359,7 +373,6 @@ extern "C" int vdit_out_modulate_unpatchify(const void* x, int64_t m, int32_t d,
     return check_launch();
 }
 
-static size_t qk_smem(int heads, int hd) { return (((size_t)3 * heads * hd * 2 + 15) & ~(size_t)15) + 4 * hd * sizeof(float); }
 
 extern "C" int vdit_qknorm_rope3d_gather(const void* qkv, int64_t n, int32_t heads, int32_t hd, const float* qs,
                                          const float* ks, const float* cs, const float* sn, int32_t res,
@@ -369,9 +382,8 @@ extern "C" int vdit_qknorm_rope3d_gather(const void* qkv, int64_t n, int32_t hea
     if (qkv == out && fwd != nullptr) return VDIT_ERR_ARG;     // a gather cannot run in place
     if (!aligned16(qkv) || !aligned16(out) || !aligned16(h_coords)) return VDIT_ERR_ALIGN;
     if (n == 0) return VDIT_OK;
-    size_t sm = qk_smem(heads, hd);
-    if (sm > 48 * 1024) return VDIT_ERR_UNSUPPORTED;
-    qknorm_rope_kernel<0><<<(unsigned)n, 128, sm, static_cast<cudaStream_t>(stream)>>>(
+    if (hd > 128) return VDIT_ERR_UNSUPPORTED;
+    qknorm_rope_kernel<0><<<blocks_for(n * heads, kQkWarps), kQkWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), n, heads, hd, qs, ks, cs, sn, res,
         reinterpret_cast<const int4*>(h_coords), fwd, 0);
     count_launches(1);
@@ -384,9 +396,8 @@ extern "C" int vdit_qknorm_rope2d(void* qkv, int64_t l, int32_t heads, int32_t h
     if (l > n_prefix && (!cs || !sn)) return VDIT_ERR_ARG;
     if (!aligned16(qkv)) return VDIT_ERR_ALIGN;
     if (l == 0) return VDIT_OK;
-    size_t sm = qk_smem(heads, hd);
-    if (sm > 48 * 1024) return VDIT_ERR_UNSUPPORTED;
-    qknorm_rope_kernel<1><<<(unsigned)l, 128, sm, static_cast<cudaStream_t>(stream)>>>(
+    if (hd > 128) return VDIT_ERR_UNSUPPORTED;
+    qknorm_rope_kernel<1><<<blocks_for(l * heads, kQkWarps), kQkWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(qkv), l, heads, hd, qs, ks, cs, sn, 1,
         nullptr, nullptr, n_prefix);
     count_launches(1);

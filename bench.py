@@ -210,6 +210,34 @@ def attention_roofline(w, runner, reps: int = 20):
     return flops, ms
 
 
+def dwconv_roofline(w, reps: int = 20):
+    """Average duration of the depthwise conv + SwiGLU kernel on the workload's shapes
+    (N=16384 shell voxels, 7680 -> 3840 channels), CUDA events on its stream.
+    Algorithmic bytes: read N*2F*2 + write N*F*2 + weights 27*2F*4 + indices N*27*4."""
+    from vdit import fast_kernels as fk
+    from vdit.workloads import shell_voxels
+    vox = torch.from_numpy(shell_voxels(w.n, w.grid, w.radius, 0)).cuda()
+    _, _, hc = fk.lex_perm(vox)
+    idx = fk.build_conv_indices_fast(hc, already_sorted=True)[0]
+    f2 = 2 * w.arch.ffn_dim
+    g = torch.Generator(device="cuda").manual_seed(2)
+    h = torch.randn(w.n, f2, device="cuda", generator=g).to(torch.bfloat16)
+    cw = 0.05 * torch.randn(27, f2, device="cuda", generator=g)
+    cb = torch.zeros(f2, device="cuda")
+    for _ in range(3):
+        fk.fast_sparse_conv3d(h, cw, cb, [idx], fuse_swiglu=True)
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for _ in range(reps):
+        fk.fast_sparse_conv3d(h, cw, cb, [idx], fuse_swiglu=True)
+    e1.record(s)
+    torch.cuda.synchronize()
+    byts = w.n * f2 * 2 + w.n * (f2 // 2) * 2 + 27 * f2 * 4 + w.n * 27 * 4
+    return byts, e0.elapsed_time(e1) / reps
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -217,6 +245,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="vdit", choices=["vdit", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="one warm-up sample, then one sample inside the NVTX range 'profile_step' (for ncu)")
+    ap.add_argument("--only", choices=["attention", "dwconv"], default=None,
+                    help="run only one kernel on the workload's shapes (small ncu case)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -234,6 +266,14 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     w = C4()
+    if args.only == "attention":
+        flops, ms = attention_roofline(w, None)
+        print(json.dumps({"kernel": "fmha_fwd_kernel<128>", "ms_per_launch": ms, "tflops": flops / ms / 1e9}))
+        return
+    if args.only == "dwconv":
+        byts, ms = dwconv_roofline(w)
+        print(json.dumps({"kernel": "dwconv27_kernel (fused SwiGLU)", "ms_per_launch": ms, "gbs": byts / ms / 1e6}))
+        return
     model = LatDitModel.random(w.arch, seed=0, device=dev)
     solver = SolverConfig(num_inference_steps=4, n_guided_steps=3, n_unguided_steps=1, guidance_scale=w.guidance)
     sol = Solution(model, solver_config=solver, device=dev)
@@ -250,6 +290,13 @@ def main():
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    if args.profile:
+        torch.cuda.nvtx.range_push("profile_step")
+        step()
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        print(json.dumps({"profile_step": "done", "launches": _lib.launch_count()}))
+        return
 
     # ---------------------------------------------------------------- timed region (device time)
     s = torch.cuda.current_stream()
