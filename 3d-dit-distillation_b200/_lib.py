@@ -21,6 +21,7 @@ _vp = ctypes.c_void_p
 SIGNATURES = {
     "vdit_version": (ctypes.c_char_p, []),
     "vdit_error_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "vdit_last_cuda_error": (ctypes.c_char_p, []),
     "vdit_launch_count": (ctypes.c_longlong, []),
     "vdit_device_error": (ctypes.c_int, [ctypes.c_int]),
     "vdit_geometry_workspace_bytes": (_c_sz, [_c_i64]),
@@ -75,7 +76,8 @@ def lib() -> ctypes.CDLL:
 def check(rc: int, what: str) -> None:
     if rc != 0:
         msg = lib().vdit_error_string(rc).decode()
-        raise RuntimeError(f"{what} failed: {msg} (code {rc})")
+        detail = lib().vdit_last_cuda_error().decode() if rc == -3 else ""
+        raise RuntimeError(f"{what} failed: {msg} (code {rc}){' ' + detail if detail else ''}")
 
 
 def stream_of(t: torch.Tensor) -> int:

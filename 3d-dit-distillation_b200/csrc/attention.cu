@@ -185,6 +185,16 @@ __device__ __forceinline__ float2 ffma2(float2 a, float s, float b) {
     return o;
 }
 
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    unsigned long long ra, rb, rd;
+    asm("mov.b64 %0, {%1,%2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
+    asm("mov.b64 %0, {%1,%2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
+    float2 o;
+    asm("mov.b64 {%0,%1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(rd));
+    return o;
+}
+
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float m;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
@@ -197,7 +207,7 @@ __device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint
     return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (layout << 61);
 }
-constexpr uint64_t kSw128 = 2, kSw64 = 4;
+constexpr uint64_t kSw64 = 4;    // layout type: 64-byte swizzle
 
 // instruction descriptor: f32 accumulate, bf16 A/B, A K-major, B K- or MN-major
 __host__ __device__ constexpr uint32_t make_idesc(int m, int n, bool b_mn_major) {
@@ -371,19 +381,19 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
                 if (!ok) break;
                 tc_fence_after();
                 const int valid = min(BN, k_len - j * BN);
-                float mt = -INFINITY;
+                float v[BN];
 #pragma unroll
-                for (int c = 0; c < BN / 32; ++c) {
-                    float v[32];
-                    tmem_ld32(tS + c * 32, v);
-                    tmem_wait_ld();
+                for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + c * 32, v + c * 32);
+                tmem_wait_ld();
+                if (valid < BN) {                               // ragged last key tile only
 #pragma unroll
-                    for (int i = 0; i < 32; i += 2) {
-                        const float a = (c * 32 + i < valid) ? v[i] : -INFINITY;
-                        const float b2 = (c * 32 + i + 1 < valid) ? v[i + 1] : -INFINITY;
-                        mt = fmax3(mt, a, b2);
-                    }
+                    for (int c = 0; c < BN; ++c)
+                        if (c >= valid) v[c] = -INFINITY;
                 }
+                float mt = fmax3(v[0], v[1], v[2]);
+#pragma unroll
+                for (int c = 3; c < BN - 1; c += 2) mt = fmax3(mt, v[c], v[c + 1]);
+                mt = fmaxf(mt, v[BN - 1]);
                 const float m_new = fmaxf(m_run, mt * scale_log2);
                 float alpha = 1.f;
                 bool rescale = false;
@@ -407,26 +417,22 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
                     }
                 }
                 // P = exp2(S*scale - m) as bf16 pairs, written over the S columns already read
-                float lsum = 0.f;
+                float2 lsum = make_float2(0.f, 0.f);
                 const float nm = -m_run;
 #pragma unroll
                 for (int c = 0; c < BN / 32; ++c) {
-                    float v[32];
-                    tmem_ld32(tS + c * 32, v);
-                    tmem_wait_ld();
                     uint32_t pk[16];
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
-                        float2 e = ffma2(make_float2(v[i], v[i + 1]), scale_log2, nm);
-                        float p0 = (c * 32 + i < valid) ? ex2(e.x) : 0.f;
-                        float p1 = (c * 32 + i + 1 < valid) ? ex2(e.y) : 0.f;
-                        lsum += p0 + p1;
-                        __nv_bfloat162 bp = __floats2bfloat162_rn(p0, p1);
+                        const float2 e = ffma2(make_float2(v[c * 32 + i], v[c * 32 + i + 1]), scale_log2, nm);
+                        const float2 p = make_float2(ex2(e.x), ex2(e.y));   // masked columns: ex2(-inf) = 0
+                        lsum = fadd2(lsum, p);
+                        __nv_bfloat162 bp = __floats2bfloat162_rn(p.x, p.y);
                         pk[i >> 1] = *reinterpret_cast<uint32_t*>(&bp);
                     }
                     tmem_st16(tS + c * 16, pk);
                 }
-                l_run += lsum;
+                l_run += lsum.x + lsum.y;
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(b_pfull(g));
@@ -502,8 +508,11 @@ int launch(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, __n
     static bool configured = false;
     const size_t sm = smem_bytes<HD>();
     if (!configured) {
-        if (cudaFuncSetAttribute(fmha_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+        const cudaError_t e = cudaFuncSetAttribute(fmha_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        if (e != cudaSuccess) {
+            record_cuda_error(e);
             return VDIT_ERR_LAUNCH;
+        }
         configured = true;
     }
     fmha_fwd_kernel<HD><<<dim3(tiles, heads), THREADS, sm, s>>>(q, k, v, out, out_stride, out_rows, seg, scale_log2);

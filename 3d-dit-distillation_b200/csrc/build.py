@@ -26,6 +26,11 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompil
          "-I", str(ROOT / "include")]
 
 
+# per-file extra flags: the attention kernel keeps a 128-column score row in
+# registers per thread (320 threads, one CTA per SM), so it may use up to 200.
+EXTRA = {"attention.cu": ["-maxrregcount=200"]}
+
+
 def _sources():
     return sorted(CSRC.glob("*.cu"))
 
@@ -39,7 +44,7 @@ def _compile(src: Path, ptxas_info: bool, verbose: bool) -> Path:
     newest_dep = max([src.stat().st_mtime] + [h.stat().st_mtime for h in _headers()])
     if obj.exists() and obj.stat().st_mtime >= newest_dep and not ptxas_info:
         return obj
-    cmd = [NVCC, *ARCH, *FLAGS, "-c", str(src), "-o", str(obj)]
+    cmd = [NVCC, *ARCH, *FLAGS, *EXTRA.get(src.name, []), "-c", str(src), "-o", str(obj)]
     if ptxas_info:
         cmd += ["-Xptxas", "-v"]
     if verbose:

@@ -14,9 +14,15 @@ void count_launches(int n);
 
 
 
+// Records the name/message of the last CUDA error seen by an entry point
+// (vdit_last_cuda_error() returns it).
+void record_cuda_error(cudaError_t e);
+
 inline int check_launch() {
     cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? VDIT_OK : VDIT_ERR_LAUNCH;
+    if (e == cudaSuccess) return VDIT_OK;
+    record_cuda_error(e);
+    return VDIT_ERR_LAUNCH;
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -128,9 +128,11 @@ int launch_dw(const void* h, int64_t n, int32_t c, const int32_t* idx, const flo
     const size_t sm = (size_t)(27 + 1) * (FUSE ? 2 : 1) * kTile * sizeof(float);
     static bool configured = false;
     if (!configured) {
-        if (cudaFuncSetAttribute(dwconv27_kernel<FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) !=
-            cudaSuccess)
+        const cudaError_t e = cudaFuncSetAttribute(dwconv27_kernel<FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        if (e != cudaSuccess) {
+            record_cuda_error(e);
             return VDIT_ERR_LAUNCH;
+        }
         configured = true;
     }
     const int64_t rows_per_cta = (int64_t)kWarps * kRowsPerWarp;

@@ -2,6 +2,7 @@
 // accounting.  The device error word lives with the kernels that set it
 // (attention.cu).
 #include <atomic>
+#include <cstdio>
 
 #include "common.cuh"
 
@@ -11,7 +12,15 @@ static std::atomic<long long> g_launches{0};
 
 void count_launches(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
+static thread_local char g_last_error[256] = "";
+
+void record_cuda_error(cudaError_t e) {
+    snprintf(g_last_error, sizeof(g_last_error), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
 }  // namespace vdit
+
+extern "C" const char* vdit_last_cuda_error(void) { return vdit::g_last_error; }
 
 extern "C" const char* vdit_version(void) { return "vdit 0.1 (sm_100a)"; }
 

@@ -36,6 +36,9 @@ typedef void* vdit_stream_t;
 /* ------------------------------------------------------------------ runtime */
 const char* vdit_version(void);
 const char* vdit_error_string(int code);
+/* Name and message of the last CUDA error an entry point of this thread saw
+ * ("" when none). */
+const char* vdit_last_cuda_error(void);
 /* Number of kernels this library has launched since load (all devices). */
 long long vdit_launch_count(void);
 /* Device error word of the current device (a bounded wait that ran out or an
