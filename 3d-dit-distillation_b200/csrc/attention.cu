@@ -26,6 +26,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace vdit {
 
@@ -33,13 +34,14 @@ __device__ int g_device_error = 0;
 
 namespace fmha {
 
+using namespace tc;
+
 constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int STAGES = 2;
 constexpr int THREADS = 320;   // TMA warp, MMA warp, 2 softmax warpgroups
 constexpr int MAXSEG = 128;
-constexpr uint32_t kSpinLimit = 1u << 22;   // try_wait polls before a wait is declared stuck
-constexpr int kErrTimeout = 0x4154;   // "AT"
+constexpr int kErrTimeout = 0x4154;   // "AT": a bounded wait of the attention kernel ran out
 
 struct SegInfo {
     int nseg;
@@ -47,173 +49,6 @@ struct SegInfo {
     int k0[MAXSEG + 1];
     int tile0[MAXSEG + 1];
 };
-
-// ---------------------------------------------------------------- PTX wrappers
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// bounded wait; false when the CTA aborted (ours or another thread's timeout)
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (*abort_flag) return false;
-    }
-    *abort_flag = 1;
-    atomicExch(&g_device_error, kErrTimeout);
-    return false;
-}
-
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
-        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
-        : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tc_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
-        : "memory");
-}
-
-// 32 lanes x 32 consecutive fp32 columns -> 32 registers per thread
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
-    uint32_t r[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i]);
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
-        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
-          "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
-          "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-        : "memory");
-}
-
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-__device__ __forceinline__ float ex2(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
-
-// D (TMEM) += A (TMEM) * B (smem descriptor)
-__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                          uint32_t accum) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
-        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum)
-        : "memory");
-}
-
-// 32 lanes x 16 consecutive 32-bit columns from 16 registers per thread
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
-        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-        : "memory");
-}
-
-// packed fp32x2 FMA: (a.x*s + b, a.y*s + b)
-__device__ __forceinline__ float2 ffma2(float2 a, float s, float b) {
-    unsigned long long ra, rs, rb, rd;
-    asm("mov.b64 %0, {%1,%2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
-    asm("mov.b64 %0, {%1,%1};" : "=l"(rs) : "f"(s));
-    asm("mov.b64 %0, {%1,%1};" : "=l"(rb) : "f"(b));
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(rd) : "l"(ra), "l"(rs), "l"(rb));
-    float2 o;
-    asm("mov.b64 {%0,%1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(rd));
-    return o;
-}
-
-__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
-    unsigned long long ra, rb, rd;
-    asm("mov.b64 %0, {%1,%2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
-    asm("mov.b64 %0, {%1,%2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
-    float2 o;
-    asm("mov.b64 {%0,%1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(rd));
-    return o;
-}
-
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-    float m;
-    asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
-    return m;
-}
-
-// Shared-memory matrix descriptors (sm_100 format: start>>4 in [0,14), LBO>>4 in
-// [16,30), SBO>>4 in [32,46), version 1 at bit 46, layout type in [61,64)).
-__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint64_t layout) {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (layout << 61);
-}
-constexpr uint64_t kSw64 = 4;    // layout type: 64-byte swizzle
-
-// instruction descriptor: f32 accumulate, bf16 A/B, A K-major, B K- or MN-major
-__host__ __device__ constexpr uint32_t make_idesc(int m, int n, bool b_mn_major) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
-           ((uint32_t)(m >> 4) << 24);
-}
 
 // ---------------------------------------------------------------- kernel
 // Two 128-row query tiles per CTA (rows q_row0 .. q_row0+255), each with its
@@ -307,7 +142,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
                     tma_load_3d(smem_u32(sQ + t * TILE + c * CHUNK), &tmQ, c * 32, head, q_row0 + t * BM, b_q);
             for (int j = 0; j < n_kv; ++j) {
                 const int st = j & 1;
-                if (j >= STAGES && !mbar_wait(b_kvempty(st), ((j - STAGES) >> 1) & 1, abort_flag)) break;
+                if (j >= STAGES && !mbar_wait(b_kvempty(st), ((j - STAGES) >> 1) & 1, abort_flag, &g_device_error, kErrTimeout)) break;
                 mbar_expect_tx(b_kvfull(st), 2 * TILE);
                 const int krow = k_begin + j * BN;
                 for (int c = 0; c < NCH; ++c)
@@ -337,7 +172,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
                               kSw64), IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
                 }
             };
-            bool ok = mbar_wait(b_q, 0, abort_flag) && mbar_wait(b_kvfull(0), 0, abort_flag);
+            bool ok = mbar_wait(b_q, 0, abort_flag, &g_device_error, kErrTimeout) && mbar_wait(b_kvfull(0), 0, abort_flag, &g_device_error, kErrTimeout);
             if (ok) {
                 tc_fence_after();
                 for (int g = 0; g < ntile; ++g) {
@@ -348,8 +183,8 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
             for (int j = 0; ok && j < n_kv; ++j) {
                 const bool more = j + 1 < n_kv;
                 for (int g = 0; g < ntile; ++g) {
-                    if (!mbar_wait(b_pfull(g), j & 1, abort_flag)) { ok = false; break; }
-                    if (g == 0 && more && !mbar_wait(b_kvfull((j + 1) & 1), ((j + 1) >> 1) & 1, abort_flag)) {
+                    if (!mbar_wait(b_pfull(g), j & 1, abort_flag, &g_device_error, kErrTimeout)) { ok = false; break; }
+                    if (g == 0 && more && !mbar_wait(b_kvfull((j + 1) & 1), ((j + 1) >> 1) & 1, abort_flag, &g_device_error, kErrTimeout)) {
                         ok = false;
                         break;
                     }
@@ -377,7 +212,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
             bool ok = true;
             for (int j = 0; j < n_kv; ++j) {
                 // every lane runs each wait, then the warp agrees, so an abort never splits the warp
-                ok = __all_sync(0xffffffffu, mbar_wait(b_sfull(g), j & 1, abort_flag));
+                ok = __all_sync(0xffffffffu, mbar_wait(b_sfull(g), j & 1, abort_flag, &g_device_error, kErrTimeout));
                 if (!ok) break;
                 tc_fence_after();
                 const int valid = min(BN, k_len - j * BN);
@@ -438,7 +273,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
                 mbar_arrive(b_pfull(g));
             }
             // -------------------------------------------------------- epilogue
-            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(b_odone(g), 0, abort_flag));
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(b_odone(g), 0, abort_flag, &g_device_error, kErrTimeout));
             if (ok) {
                 tc_fence_after();
                 const float inv = 1.f / l_run;
@@ -471,6 +306,9 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
 }
 
 // ---------------------------------------------------------------- host side
+}  // namespace fmha
+
+namespace tc {
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -483,9 +321,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     });
     return fn;
 }
+}  // namespace tc
+
+namespace fmha {
 
 bool make_map(CUtensorMap* m, const void* base, int64_t rows, int heads, int hd, int64_t row_stride) {
-    auto fn = encode_fn();
+    auto fn = tc::encode_fn();
     if (!fn) return false;
     cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)heads, (cuuint64_t)rows};
     cuuint64_t strides[2] = {(cuuint64_t)hd * 2, (cuuint64_t)row_stride * 2};
@@ -566,6 +407,10 @@ extern "C" int vdit_attention(const void* q, int64_t q_stride, const void* k, in
     return check_launch();
 }
 
+namespace vdit {
+int dense_conv_error_word(int clear);   // error word of the dense conv kernel (dense_conv.cu)
+}
+
 extern "C" int vdit_device_error(int clear) {
     int v = 0;
     if (cudaDeviceSynchronize() != cudaSuccess) return VDIT_ERR_LAUNCH;
@@ -574,5 +419,7 @@ extern "C" int vdit_device_error(int clear) {
         int z = 0;
         if (cudaMemcpyToSymbol(vdit::g_device_error, &z, sizeof(int)) != cudaSuccess) return VDIT_ERR_LAUNCH;
     }
-    return v;
+    const int d = vdit::dense_conv_error_word(clear);
+    if (d < 0) return d;
+    return v != 0 ? v : d;
 }

@@ -238,6 +238,36 @@ def dwconv_roofline(w, reps: int = 20):
     return byts, e0.elapsed_time(e1) / reps
 
 
+def dense_conv_bench(reps: int = 5):
+    """C3: dense 27-tap sparse conv, N=65536 voxels of a sphere shell (r=56) in 128^3,
+    features [N,1536] bf16, weights [27,1536,1536], fp32 accumulation.  FLOPs are
+    reported per present neighbour (2*nnz*Cin*Cout) and for all 27 taps."""
+    from vdit import fast_kernels as fk
+    from vdit.workloads import shell_voxels
+    n, cin, cout = 65536, 1536, 1536
+    vox = torch.from_numpy(shell_voxels(n, 128, 56.0, 3)).cuda()
+    _, _, hc = fk.lex_perm(vox)
+    idx = fk.build_conv_indices_fast(hc, already_sorted=True)[0]
+    nnz = int((idx >= 0).sum())
+    g = torch.Generator(device="cuda").manual_seed(3)
+    f = torch.randn(n, cin, device="cuda", generator=g).to(torch.bfloat16)
+    wt = (0.02 * torch.randn(27, cout, cin, device="cuda", generator=g)).to(torch.bfloat16)
+    b = torch.zeros(cout, device="cuda")
+    for _ in range(2):
+        fk.dense_sparse_conv3d(f, wt, b, [idx])
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for _ in range(reps):
+        fk.dense_sparse_conv3d(f, wt, b, [idx])
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    return {"kernel": "dense_conv27_kernel", "ms_per_launch": ms, "nnz": nnz,
+            "tflops_nnz": 2.0 * nnz * cin * cout / ms / 1e9, "tflops_dense27": 2.0 * 27 * n * cin * cout / ms / 1e9}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -247,7 +277,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="one warm-up sample, then one sample inside the NVTX range 'profile_step' (for ncu)")
-    ap.add_argument("--only", choices=["attention", "dwconv"], default=None,
+    ap.add_argument("--only", choices=["attention", "dwconv", "dense_conv"], default=None,
                     help="run only one kernel on the workload's shapes (small ncu case)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -269,6 +299,9 @@ def main():
     if args.only == "attention":
         flops, ms = attention_roofline(w, None)
         print(json.dumps({"kernel": "fmha_fwd_kernel<128>", "ms_per_launch": ms, "tflops": flops / ms / 1e9}))
+        return
+    if args.only == "dense_conv":
+        print(json.dumps(dense_conv_bench()))
         return
     if args.only == "dwconv":
         byts, ms = dwconv_roofline(w)

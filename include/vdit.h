@@ -161,6 +161,15 @@ int vdit_attention_1q(const void* q, const void* k, const void* v, int64_t kv_st
                       int64_t n_keys, int32_t heads, int32_t head_dim, float softmax_scale,
                       void* out, void* workspace, size_t workspace_bytes, vdit_stream_t stream);
 
+/* ------------------------------------------------------------------ sparse conv (dense) */
+/* Dense 27-tap sparse conv on tcgen05: out[n,co] = b[co] + sum_d sum_ci
+ * W[d,co,ci] f[idx[n,d],ci].  f bf16 [n,cin]; w bf16 [27,cout,cin] (the
+ * reference (3,3,3,cin,cout) weight transposed, as dense_conv_fwd_cuda does,
+ * BK/ops/libsparse/conv.cu:601-645); b fp32 [cout]; out bf16 [n,cout].
+ * cin % 64 == 0, cout % 256 == 0. */
+int vdit_dense_conv27(const void* f, int64_t n, int32_t cin, int32_t cout, const int32_t* idx,
+                      const void* w, const float* b, void* out, vdit_stream_t stream);
+
 /* ------------------------------------------------------------------ sampler glue */
 /* dst[j,:] = src[idx[j],:] for fp32 rows of width c (noise[perm], lib/fast_flow.py:2576). */
 int vdit_gather_rows_f32(const float* src, const int64_t* idx, int64_t n, int32_t c, float* dst,

@@ -250,3 +250,28 @@ def test_attention_1q(n, heads, hd):
     out = fk.attention_1q(q, kv, heads, hd)
     ref = ref_attention(q.to(torch.bfloat16)[None], kv[:, :D], kv[:, D:], [0, 1], [0, n], heads, hd)[0]
     assert rel(out, ref) < 1e-2
+
+
+# ----------------------------------------------------------------------------- dense 27-tap conv
+
+@pytest.mark.parametrize("n,cin,cout", [(700, 64, 256), (3000, 128, 512), (4096, 1536, 256)])
+def test_dense_conv27(n, cin, cout):
+    from tests.golden.make_golden import shell_voxels
+    vox = shell_voxels(n, 64, 24.0, cin)
+    _, _, hc = fk.lex_perm(torch.from_numpy(vox).to(DEV))
+    idx = fk.build_conv_indices_fast(hc, already_sorted=True)[0]
+    g = torch.Generator(device=DEV).manual_seed(n + cin)
+    f = torch.randn(n, cin, device=DEV, generator=g).to(torch.bfloat16)
+    w = (0.02 * torch.randn(3, 3, 3, cin, cout, device=DEV, generator=g)).to(torch.bfloat16).float()
+    b = 0.1 * torch.randn(cout, device=DEV, generator=g)
+    wt = w.reshape(27, cin, cout).transpose(1, 2).contiguous().to(torch.bfloat16)   # [27, cout, cin]
+    out = fk.dense_sparse_conv3d(f, wt, b, [idx])
+    ref = om.dense_conv27(f.float().cpu(), w.cpu(), b.cpu(), idx.cpu())
+    assert rel(out, ref) < 1e-2
+
+
+def test_dense_conv27_rejects_bad_shapes():
+    f = torch.zeros(10, 100, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="unsupported"):
+        fk.dense_sparse_conv3d(f, torch.zeros(27, 256, 100, device=DEV, dtype=torch.bfloat16),
+                               torch.zeros(256, device=DEV), [torch.zeros(10, 27, dtype=torch.int32, device=DEV)])
