@@ -5,6 +5,8 @@
 // (max, sum, o[head_dim]) in the caller's workspace, then a combine kernel.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace vdit {
@@ -140,6 +142,74 @@ extern "C" int vdit_attention_1q(const void* q, const void* k, const void* v, in
         static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v),
         kv_stride, n, hd, scale_log2, splits, static_cast<float*>(ws));
     attn1q_combine_kernel<<<heads, 128, 0, s>>>(static_cast<const float*>(ws), splits, hd, static_cast<__nv_bfloat16*>(out));
+    count_launches(2);
+    return check_launch();
+}
+
+// ---------------------------------------------------------------- allocation-free variant
+// Some callers cannot allocate device memory at the point where they run this
+// kernel: code being captured into a CUDA graph (an allocation inside capture
+// is either forbidden or baked into the graph), foreign-language hosts that
+// reach the library through a plain FFI and have no device allocator of their
+// own, and serving loops that must not touch the allocator between requests.
+// For them vdit_attention_1q_noalloc keeps the split-K partials in a fixed
+// file-scope device array instead of a caller workspace.  The array exists
+// once per GPU that loads the library and lives until the process exits.
+namespace vdit {
+namespace {
+
+constexpr size_t kNoAllocScratchFloats = 256 * 1024;   // 1 MiB of fp32 partials per device
+__device__ __align__(256) float g_attn1q_scratch[kNoAllocScratchFloats];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+float* g_scratch_addr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device, looked up once per
+// device (the host-side symbol is not a device address and must not reach a kernel).
+int scratch_address(float** addr) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        record_cuda_error(e);
+        return VDIT_ERR_LAUNCH;
+    }
+    if (dev < 0 || dev >= kMaxDevices) return VDIT_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (g_scratch_addr[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_attn1q_scratch);
+        if (e != cudaSuccess) {
+            record_cuda_error(e);
+            return VDIT_ERR_LAUNCH;
+        }
+        g_scratch_addr[dev] = static_cast<float*>(p);
+    }
+    *addr = g_scratch_addr[dev];
+    return VDIT_OK;
+}
+
+}  // namespace
+}  // namespace vdit
+
+extern "C" int vdit_attention_1q_noalloc(const void* q, const void* k, const void* v, int64_t kv_stride, int64_t n,
+                                         int32_t heads, int32_t hd, float scale, void* out, vdit_stream_t stream) {
+    if (!q || !k || !v || !out || heads < 1 || n < 1 || kv_stride < (int64_t)heads * hd) return VDIT_ERR_ARG;
+    if (hd % 8 || hd > 128) return VDIT_ERR_UNSUPPORTED;
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (kv_stride % 8)) return VDIT_ERR_ALIGN;
+    const int splits = choose_splits(heads, n);
+    if ((size_t)heads * splits * (2 + hd) > kNoAllocScratchFloats) return VDIT_ERR_TOO_LARGE;
+    float* ws = nullptr;
+    const int rc = scratch_address(&ws);
+    if (rc != VDIT_OK) return rc;
+    // Every slot the combine kernel reads is written by the partial kernel of the
+    // same call, so the array needs no clearing between calls.
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const float scale_log2 = scale * 1.4426950408889634f;
+    attn1q_partial_kernel<<<dim3(heads, splits), kWarps * 32, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v),
+        kv_stride, n, hd, scale_log2, splits, ws);
+    attn1q_combine_kernel<<<heads, 128, 0, s>>>(ws, splits, hd, static_cast<__nv_bfloat16*>(out));
     count_launches(2);
     return check_launch();
 }

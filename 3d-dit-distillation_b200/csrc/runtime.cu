@@ -33,6 +33,7 @@ extern "C" const char* vdit_error_string(int code) {
         case VDIT_ERR_UNSUPPORTED: return "unsupported head_dim or width";
         case VDIT_ERR_WORKSPACE: return "workspace missing or too small";
         case VDIT_ERR_DRIVER: return "CUDA driver entry point failed";
+        case VDIT_ERR_TOO_LARGE: return "size exceeds the fixed scratch of the no-alloc entry point";
         default: return "unknown error";
     }
 }

@@ -32,6 +32,7 @@ typedef void* vdit_stream_t;
 #define VDIT_ERR_UNSUPPORTED (-4)  /* head_dim / width not supported         */
 #define VDIT_ERR_WORKSPACE (-5)    /* workspace too small                    */
 #define VDIT_ERR_DRIVER (-6)       /* driver entry point (tensor maps) failed */
+#define VDIT_ERR_TOO_LARGE (-7)    /* beyond the fixed scratch of a no-alloc entry point */
 
 /* ------------------------------------------------------------------ runtime */
 const char* vdit_version(void);
@@ -160,6 +161,21 @@ size_t vdit_attention_1q_workspace_bytes(int32_t heads, int32_t head_dim, int64_
 int vdit_attention_1q(const void* q, const void* k, const void* v, int64_t kv_stride,
                       int64_t n_keys, int32_t heads, int32_t head_dim, float softmax_scale,
                       void* out, void* workspace, size_t workspace_bytes, vdit_stream_t stream);
+
+/* Same computation as vdit_attention_1q, for callers that cannot allocate
+ * device memory (a region being captured into a CUDA graph, an FFI host with no
+ * device allocator, a serving loop that must not touch the allocator).  No
+ * counterpart in the reference: it is an addition of this library.  The split-K
+ * partials live in a fixed 1 MiB device array inside the library (one per GPU
+ * that loads it, kept until process exit); heads * splits * (head_dim + 2) fp32
+ * values must fit, else VDIT_ERR_TOO_LARGE (12 heads x 128 fits any n_keys).
+ * The first call on a device looks up the array's device address (make that
+ * call before any stream capture).  Calls share the array: calls that overlap
+ * on the GPU (different streams, or different threads on one device) race.
+ * Allocates nothing; q, k, v, out as for vdit_attention_1q. */
+int vdit_attention_1q_noalloc(const void* q, const void* k, const void* v, int64_t kv_stride,
+                              int64_t n_keys, int32_t heads, int32_t head_dim, float softmax_scale,
+                              void* out, vdit_stream_t stream);
 
 /* ------------------------------------------------------------------ sparse conv (dense) */
 /* Dense 27-tap sparse conv on tcgen05: out[n,co] = b[co] + sum_d sum_ci
