@@ -79,15 +79,17 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
     uint8_t* sK = sQ + 2 * TILE;                 // [STAGES]
     uint8_t* sV = sK + STAGES * TILE;            // [STAGES]
     uint64_t* bars = reinterpret_cast<uint64_t*>(sV + STAGES * TILE);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const uint32_t b_q = smem_u32(&bars[0]);
-    auto b_kvfull = [&](int s) { return smem_u32(&bars[1 + s]); };
-    auto b_kvempty = [&](int s) { return smem_u32(&bars[3 + s]); };
-    auto b_sfull = [&](int g) { return smem_u32(&bars[5 + g]); };
-    auto b_pfull = [&](int g) { return smem_u32(&bars[7 + g]); };
-    auto b_odone = [&](int g) { return smem_u32(&bars[9 + g]); };
+    auto b_kfull = [&](int s) { return smem_u32(&bars[1 + s]); };
+    auto b_kempty = [&](int s) { return smem_u32(&bars[3 + s]); };
+    auto b_vfull = [&](int s) { return smem_u32(&bars[5 + s]); };
+    auto b_vempty = [&](int s) { return smem_u32(&bars[7 + s]); };
+    auto b_sfull = [&](int g) { return smem_u32(&bars[9 + g]); };
+    auto b_pfull = [&](int g) { return smem_u32(&bars[11 + g]); };
+    auto b_odone = [&](int g) { return smem_u32(&bars[13 + g]); };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int head = blockIdx.y;
@@ -112,8 +114,10 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
     if (threadIdx.x == 0) {
         mbar_init(b_q, 1);
         for (int i = 0; i < 2; ++i) {
-            mbar_init(b_kvfull(i), 1);
-            mbar_init(b_kvempty(i), 1);
+            mbar_init(b_kfull(i), 1);
+            mbar_init(b_kempty(i), 1);
+            mbar_init(b_vfull(i), 1);
+            mbar_init(b_vempty(i), 1);
             mbar_init(b_sfull(i), 1);
             mbar_init(b_pfull(i), 128);
             mbar_init(b_odone(i), 1);
@@ -140,15 +144,23 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
             for (int t = 0; t < (has1 ? 2 : 1); ++t)
                 for (int c = 0; c < NCH; ++c)
                     tma_load_3d(smem_u32(sQ + t * TILE + c * CHUNK), &tmQ, c * 32, head, q_row0 + t * BM, b_q);
+            // K and V rings with their own barriers: K(j) is free once both S(j) are done,
+            // V(j) once both PV(j) are done, so the next K tile can load well before it is needed
             for (int j = 0; j < n_kv; ++j) {
                 const int st = j & 1;
-                if (j >= STAGES && !mbar_wait(b_kvempty(st), ((j - STAGES) >> 1) & 1, abort_flag, &g_device_error, kErrTimeout)) break;
-                mbar_expect_tx(b_kvfull(st), 2 * TILE);
                 const int krow = k_begin + j * BN;
+                if (j >= STAGES &&
+                    !mbar_wait(b_kempty(st), ((j - STAGES) >> 1) & 1, abort_flag, &g_device_error, kErrTimeout))
+                    break;
+                mbar_expect_tx(b_kfull(st), TILE);
                 for (int c = 0; c < NCH; ++c)
-                    tma_load_3d(smem_u32(sK + st * TILE + c * CHUNK), &tmK, c * 32, head, krow, b_kvfull(st));
+                    tma_load_3d(smem_u32(sK + st * TILE + c * CHUNK), &tmK, c * 32, head, krow, b_kfull(st));
+                if (j >= STAGES &&
+                    !mbar_wait(b_vempty(st), ((j - STAGES) >> 1) & 1, abort_flag, &g_device_error, kErrTimeout))
+                    break;
+                mbar_expect_tx(b_vfull(st), TILE);
                 for (int c = 0; c < NCH; ++c)
-                    tma_load_3d(smem_u32(sV + st * TILE + c * CHUNK), &tmV, c * 32, head, krow, b_kvfull(st));
+                    tma_load_3d(smem_u32(sV + st * TILE + c * CHUNK), &tmV, c * 32, head, krow, b_vfull(st));
             }
         }
     } else if (warp == 1) {
@@ -172,32 +184,53 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
                               kSw64), IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
                 }
             };
-            bool ok = mbar_wait(b_q, 0, abort_flag, &g_device_error, kErrTimeout) && mbar_wait(b_kvfull(0), 0, abort_flag, &g_device_error, kErrTimeout);
+            auto wait = [&](uint32_t bar, uint32_t parity) {
+                return mbar_wait(bar, parity, abort_flag, &g_device_error, kErrTimeout);
+            };
+            bool ok = wait(b_q, 0) && wait(b_kfull(0), 0);
             if (ok) {
                 tc_fence_after();
                 for (int g = 0; g < ntile; ++g) {
                     issue_s(g, 0);
                     tc_commit(b_sfull(g));
                 }
+                tc_commit(b_kempty(0));
             }
             for (int j = 0; ok && j < n_kv; ++j) {
                 const bool more = j + 1 < n_kv;
-                for (int g = 0; g < ntile; ++g) {
-                    if (!mbar_wait(b_pfull(g), j & 1, abort_flag, &g_device_error, kErrTimeout)) { ok = false; break; }
-                    if (g == 0 && more && !mbar_wait(b_kvfull((j + 1) & 1), ((j + 1) >> 1) & 1, abort_flag, &g_device_error, kErrTimeout)) {
+                // tile 0: PV0(j) then S0(j+1)
+                if (!wait(b_pfull(0), j & 1) || !wait(b_vfull(j & 1), (j >> 1) & 1) ||
+                    (more && !wait(b_kfull((j + 1) & 1), ((j + 1) >> 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                issue_pv(0, j);
+                if (more) {
+                    issue_s(0, j + 1);
+                    tc_commit(b_sfull(0));
+                } else {
+                    tc_commit(b_odone(0));
+                }
+                // tile 1: PV1(j) then S1(j+1)
+                if (ntile > 1) {
+                    if (!wait(b_pfull(1), j & 1)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    issue_pv(g, j);
+                    issue_pv(1, j);
+                }
+                tc_commit(b_vempty(j & 1));
+                if (ntile > 1) {
                     if (more) {
-                        issue_s(g, j + 1);
-                        tc_commit(b_sfull(g));
+                        issue_s(1, j + 1);
+                        tc_commit(b_sfull(1));
                     } else {
-                        tc_commit(b_odone(g));
+                        tc_commit(b_odone(1));
                     }
                 }
-                if (ok) tc_commit(b_kvempty(j & 1));
+                if (more) tc_commit(b_kempty((j + 1) & 1));
             }
         }
     } else {
@@ -225,10 +258,15 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
                     for (int c = 0; c < BN; ++c)
                         if (c >= valid) v[c] = -INFINITY;
                 }
-                float mt = fmax3(v[0], v[1], v[2]);
+                // row max as four independent chains (the reduction is latency-bound otherwise)
+                float mq[4];
 #pragma unroll
-                for (int c = 3; c < BN - 1; c += 2) mt = fmax3(mt, v[c], v[c + 1]);
-                mt = fmaxf(mt, v[BN - 1]);
+                for (int q = 0; q < 4; ++q) mq[q] = fmaxf(v[q], v[q + 4]);
+#pragma unroll
+                for (int c = 8; c < BN; c += 8)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) mq[q] = fmax3(mq[q], v[c + q], v[c + q + 4]);
+                const float mt = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
                 const float m_new = fmaxf(m_run, mt * scale_log2);
                 float alpha = 1.f;
                 bool rescale = false;
@@ -252,7 +290,8 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
                     }
                 }
                 // P = exp2(S*scale - m) as bf16 pairs, written over the S columns already read
-                float2 lsum = make_float2(0.f, 0.f);
+                float2 lsum[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                                  make_float2(0.f, 0.f)};   // independent partial sums
                 const float nm = -m_run;
 #pragma unroll
                 for (int c = 0; c < BN / 32; ++c) {
@@ -261,13 +300,14 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
                     for (int i = 0; i < 32; i += 2) {
                         const float2 e = ffma2(make_float2(v[c * 32 + i], v[c * 32 + i + 1]), scale_log2, nm);
                         const float2 p = make_float2(ex2(e.x), ex2(e.y));   // masked columns: ex2(-inf) = 0
-                        lsum = fadd2(lsum, p);
+                        lsum[(i >> 1) & 3] = fadd2(lsum[(i >> 1) & 3], p);
                         __nv_bfloat162 bp = __floats2bfloat162_rn(p.x, p.y);
                         pk[i >> 1] = *reinterpret_cast<uint32_t*>(&bp);
                     }
                     tmem_st16(tS + c * 16, pk);
                 }
-                l_run += lsum.x + lsum.y;
+                l_run += (lsum[0].x + lsum[0].y) + (lsum[1].x + lsum[1].y) + (lsum[2].x + lsum[2].y) +
+                         (lsum[3].x + lsum[3].y);
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(b_pfull(g));
@@ -340,7 +380,7 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int heads, int hd,
 
 template <int HD>
 size_t smem_bytes() {
-    return 1024 + (size_t)HD * 256 * (2 + 2 * STAGES) + 128;
+    return 1024 + (size_t)HD * 256 * (2 + 2 * STAGES) + 256;   // tiles + 16 barriers + TMEM slot + abort flag
 }
 
 template <int HD>

@@ -169,6 +169,38 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
     return o;
 }
 
+// packed fp32x2 FMA with vector operands: a*b + c
+__device__ __forceinline__ float2 ffma2v(float2 a, float2 b, float2 c) {
+    unsigned long long ra, rb, rc, rd;
+    asm("mov.b64 %0, {%1,%2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
+    asm("mov.b64 %0, {%1,%2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
+    asm("mov.b64 %0, {%1,%2};" : "=l"(rc) : "f"(c.x), "f"(c.y));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(rd) : "l"(ra), "l"(rb), "l"(rc));
+    float2 o;
+    asm("mov.b64 {%0,%1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(rd));
+    return o;
+}
+
+// 2^x on the FMA pipe (for x <= ~16), to take part of the exponentials off
+// the MUFU unit.  Range reduction x = j + f with j = round(x) (magic-number
+// add), f in [-1/2, 1/2]; 2^f from a degree-3 polynomial fitted here by
+// relative-error least squares on Chebyshev nodes (max rel. error 1.2e-4,
+// below the bf16 rounding the probabilities get next); 2^j is added to the
+// exponent field.  x is clamped at -126 so the exponent never wraps.
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+    constexpr float kMagic = 12582912.0f;          // 1.5 * 2^23
+    x.x = fmaxf(x.x, -126.f);
+    x.y = fmaxf(x.y, -126.f);
+    const float2 t = fadd2(x, make_float2(kMagic, kMagic));
+    const float2 j = fadd2(t, make_float2(-kMagic, -kMagic));
+    const float2 f = ffma2v(j, make_float2(-1.f, -1.f), x);
+    float2 p = ffma2v(f, make_float2(0.05459282547f, 0.05459282547f), make_float2(0.24221783876f, 0.24221783876f));
+    p = ffma2v(p, f, make_float2(0.69336861372f, 0.69336861372f));
+    p = ffma2v(p, f, make_float2(1.f, 1.f));
+    return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                       __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float m;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
