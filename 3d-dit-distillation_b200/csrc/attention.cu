@@ -14,8 +14,8 @@
 //               an optional row scatter.
 // While one tile's softmax runs, the tensor core works on the other tile.
 // Shared-memory operands use the canonical UMMA layouts: Q/K K-major with 64-byte
-// swizzle (TMA boxes of 32 channels), V MN-major with 64-byte swizzle.  No cluster
-// multicast is used anywhere.  Every mbarrier wait is bounded; a wait that runs
+// swizzle (TMA boxes of 32 channels), V MN-major with 64-byte swizzle.  Every TMA
+// load fills only this CTA's shared memory.  Every mbarrier wait is bounded; a wait that runs
 // out records an error in g_device_error, raises a CTA abort flag and the CTA
 // skips to its teardown (TMEM is always freed).
 #include <cuda.h>

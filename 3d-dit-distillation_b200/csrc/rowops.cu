@@ -264,31 +264,41 @@ __global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ h, int64_t m, in
     store8(out + row * f + c, o);
 }
 
-// x[n, d] = xt[n,16] @ w[d,16]^T; thread -> 8 consecutive outputs of one row
-__global__ void patchify_kernel(const float* __restrict__ xt, int64_t n, const float* __restrict__ w, int d,
-                                __nv_bfloat16* __restrict__ out) {
-    int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    int dv = d >> 3;
-    if (t >= n * dv) return;
-    int64_t row = t / dv;
-    int c0 = (int)(t % dv) * 8;
-    float xin[16];
-    const float4* xp = reinterpret_cast<const float4*>(xt + row * 16);
+// x[n, d] = xt[n,16] @ w[d,16]^T.  A block owns 64 output channels for many rows:
+// their 64x16 weights sit in registers (lane = one output channel pair), each
+// warp streams rows, reading a row's 16 inputs once (broadcast) and writing
+// 64 outputs per row.
+constexpr int kPatchRows = 64;
+
+__global__ void __launch_bounds__(256) patchify_kernel(const float* __restrict__ xt, int64_t n,
+                                                       const float* __restrict__ w, int d,
+                                                       __nv_bfloat16* __restrict__ out) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c0 = blockIdx.x * 64 + lane * 2;             // this lane's two output channels
+    if (c0 >= d) return;
+    float wa[16], wb[16];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) { float4 q = __ldg(xp + i); xin[4 * i] = q.x; xin[4 * i + 1] = q.y; xin[4 * i + 2] = q.z; xin[4 * i + 3] = q.w; }
-    float o[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const float4* wp = reinterpret_cast<const float4*>(w + (int64_t)(c0 + j) * 16);
-        float s = 0.f;
+    for (int i = 0; i < 16; ++i) {
+        wa[i] = __ldg(w + (int64_t)c0 * 16 + i);
+        wb[i] = __ldg(w + (int64_t)(c0 + 1) * 16 + i);
+    }
+    const int64_t r0 = (int64_t)blockIdx.y * kPatchRows;
+    for (int64_t r = r0 + warp; r < min(n, r0 + kPatchRows); r += 8) {
+        const float4* xp = reinterpret_cast<const float4*>(xt + r * 16);
+        float x[16];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            float4 q = __ldg(wp + i);
-            s += xin[4 * i] * q.x + xin[4 * i + 1] * q.y + xin[4 * i + 2] * q.z + xin[4 * i + 3] * q.w;
+            const float4 q = __ldg(xp + i);
+            x[4 * i] = q.x; x[4 * i + 1] = q.y; x[4 * i + 2] = q.z; x[4 * i + 3] = q.w;
         }
-        o[j] = s;
+        float sa = 0.f, sb = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            sa = fmaf(x[i], wa[i], sa);
+            sb = fmaf(x[i], wb[i], sb);
+        }
+        *reinterpret_cast<__nv_bfloat162*>(out + r * d + c0) = __floats2bfloat162_rn(sa, sb);
     }
-    store8(out + row * d + c0, o);
 }
 
 __global__ void gather_rows_f32_kernel(const float* __restrict__ src, const int64_t* __restrict__ idx, int64_t n, int c,
@@ -330,8 +340,9 @@ extern "C" int vdit_patchify(const float* xt, int64_t n, const float* w, int32_t
     if (n < 0 || d <= 0 || d % 8 || !xt || !w || !x_out) return VDIT_ERR_ARG;
     if (!aligned16(xt) || !aligned16(w) || !aligned16(x_out)) return VDIT_ERR_ALIGN;
     if (n == 0) return VDIT_OK;
-    patchify_kernel<<<blocks_for(n * (d / 8), 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        xt, n, w, d, static_cast<__nv_bfloat16*>(x_out));
+    if (d % 2) return VDIT_ERR_UNSUPPORTED;
+    patchify_kernel<<<dim3((d + 63) / 64, (unsigned)((n + kPatchRows - 1) / kPatchRows)), 256, 0,
+                      static_cast<cudaStream_t>(stream)>>>(xt, n, w, d, static_cast<__nv_bfloat16*>(x_out));
     count_launches(1);
     return check_launch();
 }

@@ -18,7 +18,6 @@ host's cores instead.
 from __future__ import annotations
 
 import argparse
-import datetime
 import json
 import math
 import os
@@ -100,35 +99,6 @@ class ClockSampler:
 
 def _l2_flush(buf: torch.Tensor):
     buf.add_(1)          # 256 MiB write: larger than the 126 MB L2
-
-
-def _dist():
-    ws = int(os.environ.get("WORLD_SIZE", "1"))
-    if ws > 1:
-        import torch.distributed as dist
-        rank = int(os.environ["RANK"])
-        local = int(os.environ.get("LOCAL_RANK", rank))
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-        return dist, rank, ws, local
-    return None, 0, 1, 0
-
-
-def gather_latents(dist, lat: torch.Tensor, rank: int, ws: int):
-    """Variable-length [N_i,16] latents -> rank 0: sizes first, then a padded gather
-    (the pattern of BK/base_models/optimization_utils.py:511-535)."""
-    n = torch.tensor([lat.shape[0]], device=lat.device, dtype=torch.int64)
-    sizes = [torch.zeros_like(n) for _ in range(ws)]
-    dist.all_gather(sizes, n)
-    mx = int(max(int(s) for s in sizes))
-    pad = torch.zeros(mx, lat.shape[1], device=lat.device, dtype=lat.dtype)
-    pad[: lat.shape[0]] = lat
-    outs = [torch.empty_like(pad) for _ in range(ws)] if rank == 0 else None
-    dist.gather(pad, outs, dst=0)
-    if rank == 0:
-        return [o[: int(s)] for o, s in zip(outs, sizes)]
-    return None
 
 
 def cpu_baseline_sample(threads: int):
@@ -292,7 +262,9 @@ def main():
     from vdit.solution import Solution
     from vdit.workloads import C4
 
-    dist, rank, ws, local = _dist()
+    from vdit import distributed as vd
+    rank, ws, local = vd.init_from_env("nccl", timeout_s=120)
+    dist = torch.distributed if ws > 1 else None
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     w = C4()
@@ -317,7 +289,7 @@ def main():
     def step():
         lat = runner.sample_with_context(inp["vox"], inp["context"], noise=inp["noise"])
         if dist is not None:
-            gather_latents(dist, lat, rank, ws)
+            vd.gather_latents([lat], rank, ws)
         return lat
 
     for _ in range(args.warmup):
@@ -390,7 +362,7 @@ def main():
         lat = sol.generate([vox_h], conditioning=cond, generator=gen)[0]
         lat_h = lat.cpu()
         if dist is not None:
-            gather_latents(dist, lat, rank, ws)
+            vd.gather_latents([lat], rank, ws)
         torch.cuda.synchronize()
         e2e_ms.append((time.perf_counter() - t0) * 1e3)
     te = torch.tensor([statistics.median(e2e_ms)], device=dev)
