@@ -161,11 +161,14 @@ __global__ void __launch_bounds__(256) out_unpatchify_kernel(const __nv_bfloat16
 }
 
 // ---------------------------------------------------------------- QK norm + RoPE
-// One warp per (token row, head): lanes 0..15 hold the head's q vector, lanes
-// 16..31 its k vector (8 channels each, one 16-byte load per lane; head_dim 96
-// uses 12 lanes per half).  RMS statistics reduce over the 16-lane half with
-// shuffles; the normalised values go through a per-warp shared-memory slot so
-// each lane can read its RoPE partner channel (e +- M); v is copied through.
+// One warp per token row, looping over its heads: lanes 0..15 hold a head's q
+// vector, lanes 16..31 its k vector (8 channels each, one 16-byte load per lane;
+// head_dim 96 uses 12 lanes per half).  The token's source index, coordinates
+// and the RoPE cos/sin of each lane's 8 channels are fetched once and reused
+// for every head; the next head's vectors are loaded while the current one is
+// normalised.  RMS statistics reduce over the 16-lane half with shuffles; the
+// normalised values go through a per-warp shared-memory slot so each lane can
+// read its RoPE partner channel (e +- M); v is copied through.
 //   MODE 0: 3D RoPE, positions from h_coords[src] via the [res, hd/6] tables,
 //           optional gather src = fwd[dst].
 //   MODE 1: 2D RoPE on tokens >= n_prefix via [L-n_prefix, 2, hd/4] tables, in place.
@@ -179,43 +182,16 @@ __global__ void __launch_bounds__(kQkWarps * 32) qknorm_rope_kernel(
     int n_prefix) {
     __shared__ float snorm[kQkWarps][2][128];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t item = (int64_t)blockIdx.x * kQkWarps + warp;
-    if (item >= rows * heads) return;
-    const int64_t dst = item / heads;
-    const int h = (int)(item % heads);
+    const int64_t dst = (int64_t)blockIdx.x * kQkWarps + warp;
+    if (dst >= rows) return;
     const int64_t src = (MODE == 0 && fwd != nullptr) ? fwd[dst] : dst;
     const int D = heads * hd;
     const int half = lane >> 4, vi = lane & 15;                 // half 0 = q, 1 = k
     const bool active = vi * 8 < hd;
-    const __nv_bfloat16* irow = in + src * (int64_t)(3 * D) + (int64_t)h * hd;
-    __nv_bfloat16* orow = out + dst * (int64_t)(3 * D) + (int64_t)h * hd;
+    const __nv_bfloat16* irow = in + src * (int64_t)(3 * D);
+    __nv_bfloat16* orow = out + dst * (int64_t)(3 * D);
 
-    float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    uint4 vcopy = make_uint4(0, 0, 0, 0);
-    if (active) {
-        load8(irow + half * D + vi * 8, x);
-        if (half == 0) vcopy = *reinterpret_cast<const uint4*>(irow + 2 * D + vi * 8);
-    }
-    float ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ss += x[j] * x[j];
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float rr = rsqrtf(ss / (float)hd + 1e-6f);
-    const float* scale = (half == 0 ? qs : ks) + h * hd;
-    float* nb = snorm[warp][half];
-    if (active) {
-        const float4 s0 = __ldg(reinterpret_cast<const float4*>(scale + vi * 8));
-        const float4 s1 = __ldg(reinterpret_cast<const float4*>(scale + vi * 8 + 4));
-        const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            x[j] = bf2f(f2bf(x[j] * rr)) * sc[j];            // normalised value rounded like the reference
-            nb[vi * 8 + j] = x[j];
-        }
-    }
-    __syncwarp();
-
+    // RoPE of this lane's 8 channels (identical for every head)
     const int naxes = MODE == 0 ? 3 : 2;
     const int M = hd / (2 * naxes);
     bool rotate = true;
@@ -231,21 +207,76 @@ __global__ void __launch_bounds__(kQkWarps * 32) qknorm_rope_kernel(
         tab_row[0] = pt * 2;
         tab_row[1] = pt * 2 + 1;
     }
-    if (active) {
-        float o[8];
+    float rc[8], rs[8];
+    int partner[8];            // channel index of the RoPE partner, -1: channel passes through
+    bool lower[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int e = vi * 8 + j;
-            const int grp = e / (2 * M), off = e - grp * 2 * M;
-            o[j] = x[j];
-            if (rotate && grp < naxes) {
-                const int f = off < M ? off : off - M;
-                const float c = __ldg(cs + tab_row[grp] * M + f), s = __ldg(sn + tab_row[grp] * M + f);
-                o[j] = off < M ? x[j] * c - nb[e + M] * s : x[j] * c + nb[e - M] * s;
+    for (int j = 0; j < 8; ++j) {
+        const int e = vi * 8 + j;
+        const int grp = e / (2 * M), off = e - grp * 2 * M;
+        rc[j] = 1.f;
+        rs[j] = 0.f;
+        partner[j] = -1;
+        lower[j] = true;
+        if (active && rotate && grp < naxes) {
+            const int f = off < M ? off : off - M;
+            rc[j] = __ldg(cs + tab_row[grp] * M + f);
+            rs[j] = __ldg(sn + tab_row[grp] * M + f);
+            lower[j] = off < M;
+            partner[j] = lower[j] ? e + M : e - M;
+        }
+    }
+
+    float* nb = snorm[warp][half];
+    float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};        // lanes past head_dim must add zeros to the RMS sum
+    uint4 vcopy = make_uint4(0, 0, 0, 0);
+    if (active) {
+        load8(irow + half * D + vi * 8, x);
+        if (half == 0) vcopy = *reinterpret_cast<const uint4*>(irow + 2 * D + vi * 8);
+    }
+    for (int h = 0; h < heads; ++h) {
+        // prefetch the next head's vectors
+        float xn[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        uint4 vn = make_uint4(0, 0, 0, 0);
+        if (active && h + 1 < heads) {
+            load8(irow + half * D + (h + 1) * hd + vi * 8, xn);
+            if (half == 0) vn = *reinterpret_cast<const uint4*>(irow + 2 * D + (h + 1) * hd + vi * 8);
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += x[j] * x[j];
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float rr = rsqrtf(ss / (float)hd + 1e-6f);
+        const float* scale = (half == 0 ? qs : ks) + h * hd;
+        __syncwarp();                                    // the previous head's partner reads are done
+        if (active) {
+            const float4 s0 = __ldg(reinterpret_cast<const float4*>(scale + vi * 8));
+            const float4 s1 = __ldg(reinterpret_cast<const float4*>(scale + vi * 8 + 4));
+            const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                x[j] = bf2f(f2bf(x[j] * rr)) * sc[j];        // normalised value rounded like the reference
+                nb[vi * 8 + j] = x[j];
             }
         }
-        store8(orow + half * D + vi * 8, o);
-        if (half == 0) *reinterpret_cast<uint4*>(orow + 2 * D + vi * 8) = vcopy;
+        __syncwarp();
+        if (active) {
+            float o[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                o[j] = x[j];
+                if (partner[j] >= 0) {
+                    const float pv = nb[partner[j]];
+                    o[j] = lower[j] ? x[j] * rc[j] - pv * rs[j] : x[j] * rc[j] + pv * rs[j];
+                }
+            }
+            store8(orow + half * D + h * hd + vi * 8, o);
+            if (half == 0) *reinterpret_cast<uint4*>(orow + 2 * D + h * hd + vi * 8) = vcopy;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[j] = xn[j];
+        vcopy = vn;
     }
 }
 
@@ -394,7 +425,7 @@ extern "C" int vdit_qknorm_rope3d_gather(const void* qkv, int64_t n, int32_t hea
     if (!aligned16(qkv) || !aligned16(out) || !aligned16(h_coords)) return VDIT_ERR_ALIGN;
     if (n == 0) return VDIT_OK;
     if (hd > 128) return VDIT_ERR_UNSUPPORTED;
-    qknorm_rope_kernel<0><<<blocks_for(n * heads, kQkWarps), kQkWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+    qknorm_rope_kernel<0><<<blocks_for(n, kQkWarps), kQkWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), n, heads, hd, qs, ks, cs, sn, res,
         reinterpret_cast<const int4*>(h_coords), fwd, 0);
     count_launches(1);
@@ -408,7 +439,7 @@ extern "C" int vdit_qknorm_rope2d(void* qkv, int64_t l, int32_t heads, int32_t h
     if (!aligned16(qkv)) return VDIT_ERR_ALIGN;
     if (l == 0) return VDIT_OK;
     if (hd > 128) return VDIT_ERR_UNSUPPORTED;
-    qknorm_rope_kernel<1><<<blocks_for(l * heads, kQkWarps), kQkWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+    qknorm_rope_kernel<1><<<blocks_for(l, kQkWarps), kQkWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(qkv), l, heads, hd, qs, ks, cs, sn, 1,
         nullptr, nullptr, n_prefix);
     count_launches(1);

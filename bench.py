@@ -208,6 +208,35 @@ def dwconv_roofline(w, reps: int = 20):
     return byts, e0.elapsed_time(e1) / reps
 
 
+def qknorm_bench(w, reps: int = 20):
+    """QK-RMSNorm + 3D RoPE + Hilbert gather on the workload's shapes (N=16384, 12x128).
+    Algorithmic bytes: read + write of [N, 3, H, HD] bf16 plus the gather index."""
+    from vdit import fast_kernels as fk
+    from vdit.workloads import shell_voxels
+    vox = torch.from_numpy(shell_voxels(w.n, w.grid, w.radius, 0)).cuda()
+    _, _, hc = fk.lex_perm(vox)
+    fwd, _ = fk.hilbert4_orders(hc, 1024)
+    D, H, HD = w.arch.dim, w.arch.heads, w.arch.head_dim
+    g = torch.Generator(device="cuda").manual_seed(4)
+    qkv = torch.randn(w.n, 3 * D, device="cuda", generator=g).to(torch.bfloat16)
+    qs = torch.ones(H, HD, device="cuda")
+    cos, sin = fk.precompute_rope_3d_table(64, 128.0, HD, device="cuda")
+    out = torch.empty_like(qkv)
+    for _ in range(3):
+        fk.fused_qknorm_rope3d_gather(qkv, qs, qs, cos, sin, hc, fwd[0], H, HD, out=out)
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for _ in range(reps):
+        fk.fused_qknorm_rope3d_gather(qkv, qs, qs, cos, sin, hc, fwd[0], H, HD, out=out)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    byts = 2 * w.n * 3 * D * 2 + w.n * 8
+    return {"kernel": "qknorm_rope_kernel<0>", "ms_per_launch": ms, "gbs": byts / ms / 1e6}
+
+
 def dense_conv_bench(reps: int = 5):
     """C3: dense 27-tap sparse conv, N=65536 voxels of a sphere shell (r=56) in 128^3,
     features [N,1536] bf16, weights [27,1536,1536], fp32 accumulation.  FLOPs are
@@ -247,7 +276,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="one warm-up sample, then one sample inside the NVTX range 'profile_step' (for ncu)")
-    ap.add_argument("--only", choices=["attention", "dwconv", "dense_conv"], default=None,
+    ap.add_argument("--only", choices=["attention", "dwconv", "dense_conv", "qknorm"], default=None,
                     help="run only one kernel on the workload's shapes (small ncu case)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -271,6 +300,9 @@ def main():
     if args.only == "attention":
         flops, ms = attention_roofline(w, None)
         print(json.dumps({"kernel": "fmha_fwd_kernel<128>", "ms_per_launch": ms, "tflops": flops / ms / 1e9}))
+        return
+    if args.only == "qknorm":
+        print(json.dumps(qknorm_bench(w)))
         return
     if args.only == "dense_conv":
         print(json.dumps(dense_conv_bench()))
