@@ -449,6 +449,7 @@ extern "C" int vdit_attention(const void* q, int64_t q_stride, const void* k, in
 
 namespace vdit {
 int dense_conv_error_word(int clear);   // error word of the dense conv kernel (dense_conv.cu)
+int dwconv_plan_error_word(int clear);  // error word of the staged depthwise conv (dwconv_plan.cu)
 }
 
 extern "C" int vdit_device_error(int clear) {
@@ -461,5 +462,7 @@ extern "C" int vdit_device_error(int clear) {
     }
     const int d = vdit::dense_conv_error_word(clear);
     if (d < 0) return d;
-    return v != 0 ? v : d;
+    const int p = vdit::dwconv_plan_error_word(clear);
+    if (p < 0) return p;
+    return v != 0 ? v : (d != 0 ? d : p);
 }

@@ -186,12 +186,16 @@ class OptimizedLatDitRunner:
         order_caches = fk.build_order_caches_fast(h_coords, [N], self.arch.orders,
                                                   {"patch_size": self.arch.patch_size}, coord_bound=1024)
         conv_indices = fk.build_conv_indices_fast(h_coords, already_sorted=True)
+        # staging plan of the fused conv + SwiGLU: blocks of rows along the first Hilbert order
+        conv_plan = (fk.build_conv_plan(conv_indices, order_caches[0][0])
+                     if (2 * self.arch.ffn_dim) % 128 == 0 else None)
         L = context.shape[-2]
         cond_size = int(round(math.sqrt(max(L - 5, 0))))
         cos2, sin2 = self._get_rope_2d_table(cond_size) if L > 5 else (None, None)
         return {"N": N, "batch_size": 1, "sizes": [N], "layout": [slice(0, N)], "perm": perm, "up_widx": up_widx,
                 "h_coords": h_coords, "cos_vox": self.cos3, "sin_vox": self.sin3, "cos_cond_2d": cos2,
                 "sin_cond_2d": sin2, "order_caches": order_caches, "conv_indices": conv_indices,
+                "conv_plan": conv_plan,
                 "q_seqlens": [0, N], "q_maxlen": N, "kv_seqlens_full": [0, L], "kv_maxlen_full": L,
                 "kv_seqlens_1tok": [0, 1], "kv_maxlen_1tok": 1}
 
@@ -210,7 +214,10 @@ class OptimizedLatDitRunner:
     def _ffn(self, b: int, h_mod: torch.Tensor, geom) -> torch.Tensor:
         w = self.blocks[b]
         h2 = F.linear(h_mod, w["ffn0"], w["ffn0_b"])
-        y = fk.fast_sparse_conv3d(h2, w["conv_w"], w["conv_b"], geom["conv_indices"], fuse_swiglu=True)
+        if geom.get("conv_plan") is not None:
+            y = fk.fast_sparse_conv3d_swiglu_planned(h2, w["conv_w"], w["conv_b"], geom["conv_plan"])
+        else:
+            y = fk.fast_sparse_conv3d(h2, w["conv_w"], w["conv_b"], geom["conv_indices"], fuse_swiglu=True)
         return F.linear(y, w["ffn1"], w["ffn1_b"])
 
     @torch.no_grad()

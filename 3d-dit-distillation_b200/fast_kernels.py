@@ -217,6 +217,29 @@ def fast_swiglu_from_packed(h_packed: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def build_conv_plan(conv_indices, row_order: torch.Tensor) -> torch.Tensor:
+    """Shared-memory staging plan for the fused conv + SwiGLU, built once per
+    voxel set from the conv index table (``build_conv_indices_fast``) and a
+    Hilbert order of the rows; see ``fast_sparse_conv3d_swiglu_planned``."""
+    idx = conv_indices[0] if isinstance(conv_indices, (list, tuple)) else conv_indices
+    n = idx.shape[0]
+    order = row_order.to(torch.int64).contiguous()
+    plan = torch.empty(max(1, int(lib().vdit_dwconv27_plan_bytes(n))), dtype=torch.uint8, device=idx.device)
+    check(lib().vdit_dwconv27_plan(ptr(idx), ptr(order), n, ptr(plan), plan.numel(), _s(idx)), "dwconv27_plan")
+    return plan
+
+
+def fast_sparse_conv3d_swiglu_planned(feat: torch.Tensor, weight_fp32: torch.Tensor, bias_fp32: torch.Tensor,
+                                      plan: torch.Tensor) -> torch.Tensor:
+    """silu(conv(feat)[:, C/2:]) * conv(feat)[:, :C/2], bit-identical to
+    ``fast_sparse_conv3d(..., fuse_swiglu=True)``, from a ``build_conv_plan``."""
+    n, c = feat.shape
+    out = torch.empty(n, c // 2, dtype=BF16, device=feat.device)
+    check(lib().vdit_dwconv27_swiglu_planned(ptr(feat), n, c, ptr(plan), ptr(weight_fp32), ptr(bias_fp32),
+                                             ptr(out), _s(feat)), "dwconv27_swiglu_planned")
+    return out
+
+
 def fast_sparse_conv3d(feat: torch.Tensor, weight_fp32: torch.Tensor, bias_fp32: torch.Tensor,
                        conv_indices, fuse_swiglu: bool = False) -> torch.Tensor:
     """Depthwise 27-tap conv (``lib/fast_kernels.py:1704-1736``); with

@@ -194,18 +194,26 @@ def dwconv_roofline(w, reps: int = 20):
     h = torch.randn(w.n, f2, device="cuda", generator=g).to(torch.bfloat16)
     cw = 0.05 * torch.randn(27, f2, device="cuda", generator=g)
     cb = torch.zeros(f2, device="cuda")
-    for _ in range(3):
-        fk.fast_sparse_conv3d(h, cw, cb, [idx], fuse_swiglu=True)
-    s = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    e0.record(s)
-    for _ in range(reps):
-        fk.fast_sparse_conv3d(h, cw, cb, [idx], fuse_swiglu=True)
-    e1.record(s)
-    torch.cuda.synchronize()
+    fwd, _ = fk.hilbert4_orders(hc, 1024)
+    plan = fk.build_conv_plan([idx], fwd[0])
     byts = w.n * f2 * 2 + w.n * (f2 // 2) * 2 + 27 * f2 * 4 + w.n * 27 * 4
-    return byts, e0.elapsed_time(e1) / reps
+    s = torch.cuda.current_stream()
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(reps):
+            fn()
+        e1.record(s)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    ms_gather = timed(lambda: fk.fast_sparse_conv3d(h, cw, cb, [idx], fuse_swiglu=True))
+    ms_planned = timed(lambda: fk.fast_sparse_conv3d_swiglu_planned(h, cw, cb, plan))
+    return byts, ms_planned, ms_gather
 
 
 def qknorm_bench(w, reps: int = 20):
@@ -308,8 +316,9 @@ def main():
         print(json.dumps(dense_conv_bench()))
         return
     if args.only == "dwconv":
-        byts, ms = dwconv_roofline(w)
-        print(json.dumps({"kernel": "dwconv27_kernel (fused SwiGLU)", "ms_per_launch": ms, "gbs": byts / ms / 1e6}))
+        byts, ms, ms_gather = dwconv_roofline(w)
+        print(json.dumps({"kernel": "dwconv_planned_kernel (fused SwiGLU)", "ms_per_launch": ms,
+                          "gbs": byts / ms / 1e6, "gather_kernel_ms": ms_gather}))
         return
     model = LatDitModel.random(w.arch, seed=0, device=dev)
     solver = SolverConfig(num_inference_steps=4, n_guided_steps=3, n_unguided_steps=1, guidance_scale=w.guidance)

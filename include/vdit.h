@@ -137,6 +137,23 @@ int vdit_swiglu_packed(const void* h, int64_t m, int32_t f, void* out, vdit_stre
 int vdit_dwconv27(const void* h, int64_t n, int32_t c, const int32_t* idx, const float* w,
                   const float* b, void* out, int32_t fuse_swiglu, vdit_stream_t stream);
 
+/* The same conv with the SwiGLU fused, computed from a plan that stages each
+ * block's neighbour rows in shared memory.  The plan plays the role of the
+ * index table the reference builds once per voxel set and reuses in every
+ * block and solver step (libsparse.conv_indices, BK/ops/libsparse/conv.cu:21-163,
+ * consumed by conv_fwd, conv.cu:187-309): it is built from that table and a
+ * space-filling-curve order of the rows (row_order [n] int64, a permutation of
+ * [0,n), e.g. the Hilbert fwd order of vdit_hilbert4_orders) into a caller-owned
+ * buffer of vdit_dwconv27_plan_bytes(n) bytes, and depends on nothing else.
+ * vdit_dwconv27_swiglu_planned gives bit-identical results to vdit_dwconv27
+ * with fuse_swiglu=1 on the same idx; c must be a multiple of 128
+ * (VDIT_ERR_UNSUPPORTED otherwise). */
+size_t vdit_dwconv27_plan_bytes(int64_t n);
+int vdit_dwconv27_plan(const int32_t* idx, const int64_t* row_order, int64_t n, void* plan,
+                       size_t plan_bytes, vdit_stream_t stream);
+int vdit_dwconv27_swiglu_planned(const void* h, int64_t n, int32_t c, const void* plan,
+                                 const float* w, const float* b, void* out, vdit_stream_t stream);
+
 /* ------------------------------------------------------------------ attention */
 /* Non-causal varlen flash attention on tcgen05 tensor cores (head_dim 96 or 128).
  * Row i of segment s attends to key rows [cu_k[s], cu_k[s+1]).  q/k/v point at

@@ -52,6 +52,12 @@ def test_shape_errors_are_reported_before_any_launch():
     assert lib.vdit_modulate(None, 10, 1536, None, None, None, None) == -1
     assert lib.vdit_attention(None, 0, None, 0, None, 0, None, 0, None, None, None, 0, 12, 128, 1.0, None) == -1
     assert lib.vdit_dwconv27(None, 5, 7680, None, None, None, None, 1, None) == -1
+    assert lib.vdit_dwconv27_plan_bytes(0) == 0
+    assert lib.vdit_dwconv27_plan_bytes(129) == 2 * lib.vdit_dwconv27_plan_bytes(128)
+    assert lib.vdit_dwconv27_plan(None, None, 5, None, 0, None) == -1
+    assert lib.vdit_dwconv27_plan(16, 16, 5, 16, 0, None) == -5            # plan buffer too small
+    assert lib.vdit_dwconv27_swiglu_planned(None, 5, 7680, None, None, None, None, None) == -1
+    assert lib.vdit_dwconv27_swiglu_planned(16, 5, 960, 16, 16, 16, 16, None) == -4   # c % 128 != 0
     with pytest.raises(RuntimeError, match="invalid argument"):
         _lib.check(-1, "probe")
 

@@ -196,6 +196,57 @@ def test_dwconv27(c):
     assert rel(fk.fast_sparse_conv3d(h, w, b, [idx], fuse_swiglu=True), torch.nn.functional.silu(gg) * a) < 1e-2
 
 
+def _planned_case(vox, c, seed):
+    _, _, hc = fk.lex_perm(torch.from_numpy(vox).to(DEV))
+    idx = fk.build_conv_indices_fast(hc, already_sorted=True)[0]
+    fwd, _ = fk.hilbert4_orders(hc, 1024)
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    n = hc.shape[0]
+    h = torch.randn(n, c, device=DEV, generator=g).to(torch.bfloat16)
+    w = 0.2 * torch.randn(27, c, device=DEV, generator=g)
+    b = 0.1 * torch.randn(c, device=DEV, generator=g)
+    return h, w, b, idx, fwd
+
+
+@pytest.mark.parametrize("case", ["shell", "shell_ragged", "scattered", "cube", "tiny"])
+def test_dwconv27_swiglu_planned(case):
+    """The staged kernel equals the gather kernel bit for bit: staged blocks on a
+    surface, scattered voxels, a dense cube, a partial last block and a single
+    voxel; in lexicographic order most blocks of the shell and the cube exceed
+    the slot capacity and run from global memory."""
+    from tests.golden.make_golden import shell_voxels
+    if case == "shell":
+        vox, c = shell_voxels(16384, 64, 36.0, 0), 7680
+    elif case == "shell_ragged":
+        vox, c = shell_voxels(5001, 64, 24.0, 3), 1024
+    elif case == "scattered":
+        rng = np.random.default_rng(5)
+        vox, c = np.unique(rng.integers(0, 64, size=(3000, 3)), axis=0).astype(np.int32), 512
+    elif case == "cube":
+        g = np.meshgrid(np.arange(20), np.arange(20), np.arange(20), indexing="ij")
+        vox, c = np.stack(g, -1).reshape(-1, 3).astype(np.int32), 256
+    else:
+        vox, c = np.array([[3, 4, 5]], np.int32), 256
+    h, w, b, idx, fwd = _planned_case(vox, c, 17)
+    ref = fk.fast_sparse_conv3d(h, w, b, [idx], fuse_swiglu=True)
+    for k in (0, 2):
+        plan = fk.build_conv_plan([idx], fwd[k])
+        out = fk.fast_sparse_conv3d_swiglu_planned(h, w, b, plan)
+        assert torch.equal(out, ref), (case, k, (out.float() - ref.float()).abs().max().item())
+    # identity order: lexicographic blocks, mostly global-memory on the shell
+    plan = fk.build_conv_plan([idx], torch.arange(h.shape[0], device=DEV))
+    assert torch.equal(fk.fast_sparse_conv3d_swiglu_planned(h, w, b, plan), ref)
+
+
+def test_dwconv27_planned_vs_oracle():
+    from tests.golden.make_golden import shell_voxels
+    h, w, b, idx, fwd = _planned_case(shell_voxels(3000, 64, 20.0, 2), 768, 4)
+    ref = om.dwconv27(h.float().cpu(), w.cpu(), b.cpu(), idx.cpu())
+    a, gg = ref.chunk(2, -1)
+    plan = fk.build_conv_plan([idx], fwd[0])
+    assert rel(fk.fast_sparse_conv3d_swiglu_planned(h, w, b, plan), torch.nn.functional.silu(gg) * a) < 1e-2
+
+
 # ----------------------------------------------------------------------------- attention
 
 def ref_attention(q, k, v, cu_q, cu_k, heads, hd):
