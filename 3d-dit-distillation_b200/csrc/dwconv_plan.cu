@@ -6,28 +6,35 @@
 // bytes cross the L2->SM path while DRAM sees the input once.  Here the rows
 // are cut into blocks of 128 consecutive voxels along the Hilbert curve (a
 // compact surface patch); the union of a block's neighbours is ~1.8x its size
-// on a surface (at most ~2.8x in a dense volume, within the 384-slot capacity).
-// A plan built once per voxel set (the conv indices do not change across
-// layers or solver steps) lists, per block, the union ("slots") and, per group
-// of 4 output rows, the slot of each (row, tap) and the union of the rows'
-// valid-tap masks.  The conv kernel then copies a block's slots x one
-// 64-channel tile of a and of gate into shared memory once and computes all
-// 128 rows from there.
+// on a surface.  A plan built once per voxel set (the conv indices do not
+// change across layers or solver steps) lists, per block, the union ("slots")
+// and, per group of 4 output rows, the union of the rows' taps as a compact
+// list with the slot of each (row, tap).  Rows are grouped greedily so that a
+// group's union stays small (18.3 taps for 13.4 present per row on the shell
+// workload).  The conv kernel copies a block's slots x one 64-channel tile of
+// a and gate into shared memory once and computes all 128 rows from there.
+//
+// Layout: the packed hidden h' [n, c] is pair-interleaved -- columns
+// 4k..4k+3 hold (a[2k], a[2k+1], gate[2k], gate[2k+1]) -- and so are the conv
+// weights w' [27, c] and bias b' [c]; the output is silu(gate) * a in natural
+// channel order [n, c/2].  The runner obtains this layout for free by
+// permuting the rows of the up-projection that produces h.  A lane then reads
+// its 2 a + 2 gate values with one 8-byte load and its 4 weights with one
+// 16-byte load, and one TMA row copy covers a whole tile.
 //
 // Mapping: a persistent CTA (one per SM) walks work units (tile, block) in
-// tile-major order.  One producer warp stages unit u+1 while the 8 compute
-// warps work on unit u: TMA tile::gather4 copies four slot rows x 64 channels
-// per instruction, a bulk copy brings the group table, and an mbarrier pair per
-// stage hands the buffer over (waits are bounded; a timeout sets the device
-// error word).  The compute warps' fp32 weights (27 taps x 2 a + 2 gate
-// channels per lane) stay in registers across units of one tile.  A warp
-// computes one group of 4 rows at a time: lane l owns channels (2l, 2l+1) of
-// the tile; the 27 taps are unrolled and skipped by the group's mask
-// (warp-uniform); a row without a tap reads a zero row.  Accumulation order (bias,
-// then taps in increasing index) and fp32 FMAs match the gather kernel, so
-// results are bit-identical to it.  Blocks whose union exceeds the slot
-// capacity (scattered voxels) keep global row indices in the plan and are
-// computed from global memory.
+// tile-major order.  One producer warp stages unit u+1 while 16 compute warps
+// work on unit u: TMA tile::gather4 copies four slot rows x 128 columns per
+// instruction, bulk copies bring the group table and (when the tile changes)
+// the tile's weights, and an mbarrier pair per stage hands the buffer over
+// (waits are bounded; a timeout sets the device error word).  A warp computes
+// one group of 4 rows at a time, lane l owning output channels (2l, 2l+1) of
+// the tile; a row without one of the group's taps reads a zero row.
+// Accumulation order (bias, then taps in increasing index) and fp32 FMAs match
+// the gather kernel, so results are bit-identical to it on the de-interleaved
+// inputs.  Blocks whose union exceeds the slot capacity (dense volumes, or a
+// row order that is not a space-filling curve) keep global row indices in the
+// plan and are computed from global memory.
 #include "common.cuh"
 #include "tc.cuh"
 
@@ -40,22 +47,25 @@ constexpr int kGroups = kPlanRows / kGroupRows;
 constexpr int kSlotCap = 320;                  // staged union rows per block
 constexpr int kCand = kPlanRows * 27;          // neighbour candidates per block
 constexpr int kSortN = 4096;                   // power of two >= kCand
-constexpr int kTileCh = 64;                    // channels of a (and of gate) per tile
-constexpr int kSlotBytes = 2 * kTileCh * 2;    // a + gate, bf16
+constexpr int kTileCh = 64;                    // output channels per tile
+constexpr int kTileCols = 2 * kTileCh;         // h' columns per tile (a + gate)
+constexpr int kSlotBytes = kTileCols * 2;      // bf16
 constexpr int kWarps = 16;                     // compute warps (+1 producer warp)
 
 struct __align__(16) Group {
     int32_t rows[kGroupRows];      // output rows (-1: padding)
-    uint32_t mask;                 // union of the rows' valid-tap masks
+    int32_t ntaps;                 // taps in the group's union
     int32_t pad[3];
-    int4 slots[27];                // per tap: byte offset of the row's a part in the stage (staged)
-                                   // or its global row, -1 if absent (overflow)
+    uint8_t taps[32];              // the union's tap indices, increasing
+    int4 slots[27];                // per union tap: byte offset of each row's staged slot
+                                   // (the zero row if the row lacks the tap), or on
+                                   // overflow its global row (-1 if absent)
 };
-static_assert(sizeof(Group) == 464, "group layout");
+static_assert(sizeof(Group) == 496, "group layout");
 
 struct __align__(16) BlockHdr {
     int32_t n_slots;               // union size
-    int32_t overflow;              // 1: slots[] hold global rows, compute from global memory
+    int32_t overflow;              // 1: slots hold global rows, compute from global memory
     int32_t pad[2];
 };
 
@@ -64,18 +74,14 @@ constexpr size_t kSlotListBytes = (size_t)kSlotCap * 4;
 constexpr size_t kGroupTabBytes = (size_t)kGroups * sizeof(Group);
 constexpr size_t kBlockPlanBytes = kHdrBytes + kSlotListBytes + kGroupTabBytes;
 
-// Stage layout: slots in quads of four (one TMA gather4 per part): quad q holds
-// a rows at q*1024 + r*128 and gate rows 512 bytes further; a zero row for a
-// (and 512 bytes further for gate) follows the data; then the block's group
-// table.  After the two stages: two weight buffers (indexed by tile parity),
-// each 27 taps + bias x [64 a | 64 gate] fp32; then barriers and flags.
-constexpr int kQuads = kSlotCap / 4;
-constexpr int kQuadBytes = 4 * kSlotBytes;
-constexpr int kGateOff = 4 * kTileCh * 2;
-constexpr int kZeroOff = kQuads * kQuadBytes;
-constexpr int kStageFeat = kZeroOff + kGateOff + kTileCh * 2;
+// Stage layout: slot s at s*256 (a quad of four slots is one TMA gather4),
+// the zero row after the last slot, then the block's group table.  After the
+// two stages: two weight buffers (indexed by tile parity), each 27 taps + bias
+// x 128 fp32 columns; then barriers and flags.
+constexpr int kZeroOff = kSlotCap * kSlotBytes;
+constexpr int kStageFeat = kZeroOff + kSlotBytes;
 constexpr int kStageBytes = kStageFeat + (int)kGroupTabBytes;
-constexpr int kWRowBytes = 2 * kTileCh * 4;
+constexpr int kWRowBytes = kTileCols * 4;
 constexpr int kWBytes = 28 * kWRowBytes;
 constexpr int kWOff = 2 * kStageBytes;
 constexpr int kBarOff = kWOff + 2 * kWBytes;
@@ -101,8 +107,9 @@ __host__ __device__ inline PlanView plan_view(void* plan, int64_t blocks) {
 // ---------------------------------------------------------------- plan build
 // One CTA per block: gather the 128x27 neighbour indices, sort them (bitonic,
 // shared memory), keep the distinct ones as slots, map every (row, tap) to its
-// slot by binary search, order the rows by tap mask so that a group's union
-// stays small, and write the group records.
+// slot by binary search, group the rows greedily (seed: the remaining row with
+// the most taps; then three times the row that grows the union least; padding
+// rows last) and write the group records.
 __global__ void __launch_bounds__(512) dwconv_plan_kernel(const int32_t* __restrict__ idx,
                                                           const int64_t* __restrict__ order, int64_t n,
                                                           int64_t blocks, void* plan) {
@@ -111,9 +118,10 @@ __global__ void __launch_bounds__(512) dwconv_plan_kernel(const int32_t* __restr
     __shared__ int32_t warp_tot[16];
     __shared__ int32_t rowid[kPlanRows];
     __shared__ uint32_t mask[kPlanRows];
-    __shared__ int32_t sorted[kPlanRows];
+    __shared__ int32_t grp_row[kGroups][kGroupRows];   // positions within the block
+    __shared__ uint32_t grp_mask[kGroups];
     __shared__ int32_t n_uniq;
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t blk = blockIdx.x;
     PlanView pv = plan_view(plan, blocks);
 
@@ -134,15 +142,42 @@ __global__ void __launch_bounds__(512) dwconv_plan_kernel(const int32_t* __restr
         mask[tid] = m;
     }
     __syncthreads();
-    // rows ordered by (mask, position); padding rows last
-    if (tid < kPlanRows) {
-        auto key = [&](int r) -> uint64_t {
-            return rowid[r] < 0 ? (1ull << 40) | (uint64_t)r : ((uint64_t)mask[r] << 8) | (uint64_t)r;
-        };
-        const uint64_t mine = key(tid);
-        int rank = 0;
-        for (int j = 0; j < kPlanRows; ++j) rank += key(j) < mine;
-        sorted[rank] = tid;
+    if (warp == 0) {
+        // greedy grouping; lane l holds rows l, l+32, l+64, l+96
+        constexpr int kPerLane = kPlanRows / 32;
+        uint32_t mk[kPerLane];
+        bool real[kPerLane], left[kPerLane];
+#pragma unroll
+        for (int j = 0; j < kPerLane; ++j) {
+            mk[j] = mask[lane + 32 * j];
+            real[j] = rowid[lane + 32 * j] >= 0;
+            left[j] = true;
+        }
+        for (int g = 0; g < kGroups; ++g) {
+            uint32_t u = 0;
+            for (int q = 0; q < kGroupRows; ++q) {
+                // smallest key wins: real rows before padding; seed = most taps, then
+                // the least union growth; ties to the lowest position
+                uint32_t best = 0xffffffffu;
+#pragma unroll
+                for (int j = 0; j < kPerLane; ++j) {
+                    if (!left[j]) continue;
+                    const uint32_t r = lane + 32 * j;
+                    const uint32_t score = q == 0 ? 27u - __popc(mk[j]) : __popc(u | mk[j]);
+                    const uint32_t key = ((real[j] ? 0u : 1u) << 20) | (score << 8) | r;
+                    best = min(best, key);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
+                const int r = (int)(best & 0xff);
+#pragma unroll
+                for (int j = 0; j < kPerLane; ++j)
+                    if (r == lane + 32 * j) left[j] = false;
+                u |= mask[r];
+                if (lane == 0) grp_row[g][q] = r;
+            }
+            if (lane == 0) grp_mask[g] = u;
+        }
     }
     // bitonic sort of the candidates, ascending
     for (int size = 2; size <= kSortN; size <<= 1) {
@@ -172,7 +207,6 @@ __global__ void __launch_bounds__(512) dwconv_plan_kernel(const int32_t* __restr
         first[j] = v[j] != INT32_MAX && (k == 0 || cand[k - 1] != v[j]);
         cnt += first[j];
     }
-    const int lane = tid & 31, warp = tid >> 5;
     int incl = cnt;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -191,8 +225,8 @@ __global__ void __launch_bounds__(512) dwconv_plan_kernel(const int32_t* __restr
     __syncthreads();
     const int U = n_uniq;
     const bool overflow = U > kSlotCap;
-    // (row, tap) -> stage offset of slot p (p = position among the distinct rows),
-    // the zero quad for an absent tap; on overflow the global row itself (-1 when absent)
+    // (row, tap) -> byte offset of slot p (p = position among the distinct rows),
+    // the zero row for an absent tap; on overflow the global row itself (-1 when absent)
     for (int k = tid; k < kCand; k += blockDim.x) {
         const int32_t x = nb[k];
         int32_t s;
@@ -206,7 +240,7 @@ __global__ void __launch_bounds__(512) dwconv_plan_kernel(const int32_t* __restr
                 const int mid = (lo + hi) >> 1;
                 if (cand[mid] < x) lo = mid + 1; else hi = mid;
             }
-            s = (lo >> 2) * kQuadBytes + (lo & 3) * (kTileCh * 2);
+            s = lo * kSlotBytes;
         }
         nb[k] = s;
     }
@@ -221,21 +255,25 @@ __global__ void __launch_bounds__(512) dwconv_plan_kernel(const int32_t* __restr
     for (int s = tid; s < kSlotCap; s += blockDim.x) pv.slot_rows[blk * kSlotCap + s] = (!overflow && s < U) ? cand[s] : 0;
     Group* g = pv.groups + blk * kGroups;
     if (tid < kGroups) {
-        uint32_t m = 0;
-        for (int q = 0; q < kGroupRows; ++q) {
-            const int r = sorted[tid * kGroupRows + q];
-            g[tid].rows[q] = rowid[r];
-            if (rowid[r] >= 0) m |= mask[r];
-        }
-        g[tid].mask = m;
+        const uint32_t m = grp_mask[tid];
+        for (int q = 0; q < kGroupRows; ++q) g[tid].rows[q] = rowid[grp_row[tid][q]];
+        g[tid].ntaps = __popc(m);
         g[tid].pad[0] = g[tid].pad[1] = g[tid].pad[2] = 0;
+        int i = 0;
+        for (int d = 0; d < 27; ++d)
+            if (m & (1u << d)) g[tid].taps[i++] = (uint8_t)d;
+        for (; i < 32; ++i) g[tid].taps[i] = 0;
     }
     for (int k = tid; k < kGroups * 27 * kGroupRows; k += blockDim.x) {
-        const int gi = k / (27 * kGroupRows), d = (k / kGroupRows) % 27, q = k % kGroupRows;
-        const int r = sorted[gi * kGroupRows + q];
-        int32_t s = nb[r * 27 + d];
-        if (rowid[r] < 0) s = overflow ? -1 : kZeroOff;
-        reinterpret_cast<int32_t*>(&g[gi].slots[d])[q] = s;
+        const int gi = k / (27 * kGroupRows), i = (k / kGroupRows) % 27, q = k % kGroupRows;
+        const uint32_t m = grp_mask[gi];
+        int32_t s = overflow ? -1 : kZeroOff;
+        if (i < __popc(m)) {
+            const int d = (int)__fns(m, 0, i + 1);      // the i-th tap of the union
+            const int r = grp_row[gi][q];
+            if (rowid[r] >= 0) s = nb[r * 27 + d];
+        }
+        reinterpret_cast<int32_t*>(&g[gi].slots[i])[q] = s;
     }
 }
 
@@ -247,13 +285,7 @@ __device__ __forceinline__ float2 unpack_bf2(uint32_t v) {
     return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
 }
 
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-    uint32_t v;
-    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
-    return v;
-}
-
-// four rows x 64 bf16 columns of h -> 512 contiguous bytes of shared memory
+// four rows x 128 bf16 columns of h' -> 1024 contiguous bytes of shared memory
 __device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, int col, int4 rows, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
@@ -269,48 +301,41 @@ __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_
                  : "memory");
 }
 
-// Accumulates one group of 4 rows over the union of their taps (ffs walk over
-// the mask; the next tap's slots are fetched while the current one computes).
+// Accumulates one group of 4 rows over its union taps; the next tap's slots
+// and index are fetched while the current one computes.
 template <bool GLOBAL>
-__device__ __forceinline__ void accumulate_group(const char* grp, const char* feat, const char* wb, int lane,
-                                                 const __nv_bfloat16* __restrict__ hcol, int c, int half,
+__device__ __forceinline__ void accumulate_group(const Group* grp, const char* feat, const char* wb, int lane,
+                                                 const __nv_bfloat16* __restrict__ hcol, int c,
                                                  float2 (&acc_a)[kGroupRows], float2 (&acc_g)[kGroupRows]) {
-    uint32_t m = reinterpret_cast<const Group*>(grp)->mask;
-    const int4* slots = reinterpret_cast<const Group*>(grp)->slots;
-    const char* fl = feat + lane * 4;
-    const char* wl = wb + lane * 8;
-    int d = __ffs(m) - 1;
-    m &= m - 1;
-    int4 sl = slots[d];
-    while (true) {
+    const int nt = grp->ntaps;
+    const char* fl = feat + lane * 8;
+    const char* wl = wb + lane * 16;
+    int4 sl = grp->slots[0];
+    int d = grp->taps[0];
+    for (int i = 0; i < nt; ++i) {
         const int s[kGroupRows] = {sl.x, sl.y, sl.z, sl.w};
-        uint32_t va[kGroupRows], vg[kGroupRows];
+        uint2 v[kGroupRows];
 #pragma unroll
         for (int q = 0; q < kGroupRows; ++q) {
             if (GLOBAL) {
                 const bool ok = s[q] >= 0;
-                const __nv_bfloat16* p = hcol + (int64_t)(ok ? s[q] : 0) * c;
-                va[q] = ok ? __ldg(reinterpret_cast<const uint32_t*>(p)) : 0u;
-                vg[q] = ok ? __ldg(reinterpret_cast<const uint32_t*>(p + half)) : 0u;
+                const uint2* p = reinterpret_cast<const uint2*>(hcol + (int64_t)(ok ? s[q] : 0) * c);
+                v[q] = ok ? __ldg(p) : make_uint2(0u, 0u);
             } else {
-                va[q] = *reinterpret_cast<const uint32_t*>(fl + s[q]);
-                vg[q] = *reinterpret_cast<const uint32_t*>(fl + s[q] + kGateOff);
+                v[q] = *reinterpret_cast<const uint2*>(fl + s[q]);
             }
         }
-        const float2 wa = *reinterpret_cast<const float2*>(wl + d * kWRowBytes);
-        const float2 wg = *reinterpret_cast<const float2*>(wl + d * kWRowBytes + kTileCh * 4);
-        const bool more = m != 0;
-        const int dn = more ? __ffs(m) - 1 : d;
-        m &= m - 1;
-        const int4 sln = slots[dn];
+        const float4 wv = *reinterpret_cast<const float4*>(wl + d * kWRowBytes);
+        // slots[27] / taps[27] past the last tap are in bounds of the record or the next
+        // one and are never used
+        sl = grp->slots[i + 1];
+        d = grp->taps[i + 1];
+        const float2 wa = make_float2(wv.x, wv.y), wg = make_float2(wv.z, wv.w);
 #pragma unroll
         for (int q = 0; q < kGroupRows; ++q) {
-            acc_a[q] = tc::ffma2v(unpack_bf2(va[q]), wa, acc_a[q]);
-            acc_g[q] = tc::ffma2v(unpack_bf2(vg[q]), wg, acc_g[q]);
+            acc_a[q] = tc::ffma2v(unpack_bf2(v[q].x), wa, acc_a[q]);
+            acc_g[q] = tc::ffma2v(unpack_bf2(v[q].y), wg, acc_g[q]);
         }
-        if (!more) break;
-        d = dn;
-        sl = sln;
     }
 }
 
@@ -325,7 +350,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) dwconv_planned_kernel(
     const PlanView pv = plan_view(const_cast<void*>(plan), blocks);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int half = c / 2;
-    const int64_t tiles = half / kTileCh;
+    const int64_t tiles = c / kTileCols;
     const int64_t units = blocks * tiles;
     const int64_t u0 = units * blockIdx.x / gridDim.x;
     const int64_t u1 = units * (blockIdx.x + 1) / gridDim.x;
@@ -345,8 +370,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) dwconv_planned_kernel(
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     // the zero rows of both stages (absent taps read them)
-    for (int k = tid; k < 2 * (kStageFeat - kZeroOff) / 16; k += blockDim.x) {
-        const int per = (kStageFeat - kZeroOff) / 16;
+    for (int k = tid; k < 2 * kSlotBytes / 16; k += blockDim.x) {
+        constexpr int per = kSlotBytes / 16;
         reinterpret_cast<uint4*>(smem + (k / per) * kStageBytes + kZeroOff)[k % per] = make_uint4(0, 0, 0, 0);
     }
     __syncthreads();
@@ -367,10 +392,10 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) dwconv_planned_kernel(
             const int nq = hd.overflow ? 0 : (hd.n_slots + 3) / 4;
             const bool new_w = tile != w_tile;
             const uint32_t dst = sbase + st * kStageBytes;
-            const int col = (int)(tile * kTileCh);
+            const int col = (int)(tile * kTileCols);
             if (lane == 0) {
                 info[st] = hd.overflow;
-                mbar_expect_tx(full(st), (uint32_t)kGroupTabBytes + (uint32_t)nq * kQuadBytes +
+                mbar_expect_tx(full(st), (uint32_t)kGroupTabBytes + (uint32_t)nq * 4 * kSlotBytes +
                                              (new_w ? (uint32_t)kWBytes : 0u));
                 bulk_copy(dst + kStageFeat, pv.groups + blk * kGroups, (uint32_t)kGroupTabBytes, full(st));
             }
@@ -378,16 +403,12 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) dwconv_planned_kernel(
             if (new_w && lane < 28) {
                 const uint32_t wdst = sbase + kWOff + (uint32_t)(tile & 1) * kWBytes + lane * kWRowBytes;
                 const float* src = lane < 27 ? w + (int64_t)lane * c : b;
-                bulk_copy(wdst, src + col, kTileCh * 4, full(st));
-                bulk_copy(wdst + kTileCh * 4, src + half + col, kTileCh * 4, full(st));
+                bulk_copy(wdst, src + col, kWRowBytes, full(st));
             }
             w_tile = tile;
             const int4* rows4 = reinterpret_cast<const int4*>(pv.slot_rows + blk * kSlotCap);
-            for (int q = lane; q < nq; q += 32) {
-                const int4 r = __ldg(rows4 + q);
-                tma_gather4(dst + q * kQuadBytes, &hmap, col, r, full(st));
-                tma_gather4(dst + q * kQuadBytes + kGateOff, &hmap, half + col, r, full(st));
-            }
+            for (int q = lane; q < nq; q += 32)
+                tma_gather4(dst + q * 4 * kSlotBytes, &hmap, col, __ldg(rows4 + q), full(st));
         }
         // nothing may still be landing in shared memory when the CTA exits
         if (lane == 0)
@@ -404,26 +425,26 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) dwconv_planned_kernel(
                                                kErrTimeout)))
             break;
         const int64_t tile = u / blocks;
-        const int64_t ch = tile * kTileCh + lane * 2;
         const bool overflow = info[st] != 0;
         const char* feat = smem + st * kStageBytes;
         const char* wb = smem + kWOff + (tile & 1) * kWBytes;
-        const float2 ba = *reinterpret_cast<const float2*>(wb + 27 * kWRowBytes + lane * 8);
-        const float2 bg = *reinterpret_cast<const float2*>(wb + 27 * kWRowBytes + kTileCh * 4 + lane * 8);
+        const float4 bias = *reinterpret_cast<const float4*>(wb + 27 * kWRowBytes + lane * 16);
+        const __nv_bfloat16* hcol = h + tile * kTileCols + lane * 4;
+        __nv_bfloat16* ocol = out + tile * kTileCh + lane * 2;
         for (int gi = warp; gi < kGroups; gi += kWarps) {
-            const char* grp = feat + kStageFeat + gi * sizeof(Group);
-            const int4 rows4 = *reinterpret_cast<const int4*>(grp);
+            const Group* grp = reinterpret_cast<const Group*>(feat + kStageFeat) + gi;
+            const int4 rows4 = *reinterpret_cast<const int4*>(grp->rows);
             if (rows4.x < 0) continue;
             float2 acc_a[kGroupRows], acc_g[kGroupRows];
 #pragma unroll
             for (int q = 0; q < kGroupRows; ++q) {
-                acc_a[q] = ba;
-                acc_g[q] = bg;
+                acc_a[q] = make_float2(bias.x, bias.y);
+                acc_g[q] = make_float2(bias.z, bias.w);
             }
             if (overflow)
-                accumulate_group<true>(grp, feat, wb, lane, h + ch, c, half, acc_a, acc_g);
+                accumulate_group<true>(grp, feat, wb, lane, hcol, c, acc_a, acc_g);
             else
-                accumulate_group<false>(grp, feat, wb, lane, h + ch, c, half, acc_a, acc_g);
+                accumulate_group<false>(grp, feat, wb, lane, hcol, c, acc_a, acc_g);
             const int rows[kGroupRows] = {rows4.x, rows4.y, rows4.z, rows4.w};
 #pragma unroll
             for (int q = 0; q < kGroupRows; ++q) {
@@ -431,8 +452,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) dwconv_planned_kernel(
                 // the conv output is rounded to bf16 before the SwiGLU reads it
                 const float a0 = bf2f(f2bf(acc_a[q].x)), a1 = bf2f(f2bf(acc_a[q].y));
                 const float g0 = bf2f(f2bf(acc_g[q].x)), g1 = bf2f(f2bf(acc_g[q].y));
-                __nv_bfloat162 o = __floats2bfloat162_rn(silu(g0) * a0, silu(g1) * a1);
-                *reinterpret_cast<__nv_bfloat162*>(out + (int64_t)rows[q] * half + ch) = o;
+                *reinterpret_cast<__nv_bfloat162*>(ocol + (int64_t)rows[q] * half) =
+                    __floats2bfloat162_rn(silu(g0) * a0, silu(g1) * a1);
             }
         }
         __syncwarp();
@@ -480,7 +501,7 @@ extern "C" int vdit_dwconv27_plan(const int32_t* idx, const int64_t* row_order, 
 extern "C" int vdit_dwconv27_swiglu_planned(const void* h, int64_t n, int32_t c, const void* plan, const float* w,
                                             const float* b, void* out, vdit_stream_t stream) {
     if (n < 0 || c <= 0 || (n > 0 && (!h || !plan || !w || !b || !out))) return VDIT_ERR_ARG;
-    if (c % (2 * kTileCh)) return VDIT_ERR_UNSUPPORTED;
+    if (c % kTileCols) return VDIT_ERR_UNSUPPORTED;
     if (n == 0) return VDIT_OK;
     if (n > INT32_MAX) return VDIT_ERR_UNSUPPORTED;
     if (!aligned16(h) || !aligned16(plan) || !aligned16(w) || !aligned16(b) || ((uintptr_t)out & 3u))
@@ -505,18 +526,18 @@ extern "C" int vdit_dwconv27_swiglu_planned(const void* h, int64_t n, int32_t c,
     }
     auto fn = tc::encode_fn();
     if (!fn) return VDIT_ERR_DRIVER;
-    // h as [n rows, c columns] bf16; one-row boxes of 64 columns (tile::gather4)
+    // h' as [n rows, c columns] bf16; one-row boxes of 128 columns (tile::gather4)
     CUtensorMap m;
     cuuint64_t dims[2] = {(cuuint64_t)c, (cuuint64_t)n};
     cuuint64_t strides[1] = {(cuuint64_t)c * 2};
-    cuuint32_t box[2] = {kTileCh, 1};
+    cuuint32_t box[2] = {kTileCols, 1};
     cuuint32_t es[2] = {1, 1};
     if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(h), dims, strides, box, es,
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return VDIT_ERR_DRIVER;
     const int64_t blocks = (n + kPlanRows - 1) / kPlanRows;
-    const int64_t units = blocks * (c / 2 / kTileCh);
+    const int64_t units = blocks * (c / kTileCols);
     const int grid = (int)(units < g_sm_count[dev] ? units : g_sm_count[dev]);
     dwconv_planned_kernel<<<grid, (kWarps + 1) * 32, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
         m, static_cast<const __nv_bfloat16*>(h), c, plan, blocks, w, b, static_cast<__nv_bfloat16*>(out));

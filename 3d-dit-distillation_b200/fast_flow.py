@@ -95,6 +95,9 @@ class OptimizedLatDitRunner:
         self.W_cg2 = torch.cat([f32(f"flow.blocks.{b}.cond_gates.weight") for b in nc]) if a.depth > cd else None
         self.b_cg2 = torch.cat([f32(f"flow.blocks.{b}.cond_gates.bias") for b in nc]) if a.depth > cd else None
 
+        Fh = a.ffn_dim
+        self.ffn_interleaved = (2 * Fh) % 128 == 0
+        self.ffn_perm = torch.arange(2 * Fh, device=self.device).view(2, Fh // 2, 2).permute(1, 0, 2).reshape(-1)
         self.blocks: List[Dict[str, torch.Tensor]] = []
         for b in range(a.depth):
             p = f"flow.blocks.{b}."
@@ -102,6 +105,13 @@ class OptimizedLatDitRunner:
             w.update({n + "_b": bf(p + n + ".bias") for n in ("to_qkv", "to_out", "to_out_cross", "ffn0", "ffn1")})
             w["conv_w"] = f32(p + "ffn_conv.weight").reshape(27, -1).contiguous()
             w["conv_b"] = f32(p + "ffn_conv.bias")
+            if self.ffn_interleaved:
+                # hidden columns (a[2k], a[2k+1], gate[2k], gate[2k+1]): the layout the staged
+                # conv reads; only the order of ffn0's outputs changes
+                w["ffn0"] = w["ffn0"][self.ffn_perm].contiguous()
+                w["ffn0_b"] = w["ffn0_b"][self.ffn_perm].contiguous()
+                w["conv_w"] = w["conv_w"][:, self.ffn_perm].contiguous()
+                w["conv_b"] = w["conv_b"][self.ffn_perm].contiguous()
             w["qs"], w["ks"] = f32(p + "qk_norm.q_scale"), f32(p + "qk_norm.k_scale")
             if b < cd:
                 for n in ("cond_to_qkv", "cond_to_out", "to_qkv_cross", "cond_to_qkv_cross", "cond_to_out_cross",
@@ -187,8 +197,7 @@ class OptimizedLatDitRunner:
                                                   {"patch_size": self.arch.patch_size}, coord_bound=1024)
         conv_indices = fk.build_conv_indices_fast(h_coords, already_sorted=True)
         # staging plan of the fused conv + SwiGLU: blocks of rows along the first Hilbert order
-        conv_plan = (fk.build_conv_plan(conv_indices, order_caches[0][0])
-                     if (2 * self.arch.ffn_dim) % 128 == 0 else None)
+        conv_plan = fk.build_conv_plan(conv_indices, order_caches[0][0]) if self.ffn_interleaved else None
         L = context.shape[-2]
         cond_size = int(round(math.sqrt(max(L - 5, 0))))
         cos2, sin2 = self._get_rope_2d_table(cond_size) if L > 5 else (None, None)
@@ -214,7 +223,7 @@ class OptimizedLatDitRunner:
     def _ffn(self, b: int, h_mod: torch.Tensor, geom) -> torch.Tensor:
         w = self.blocks[b]
         h2 = F.linear(h_mod, w["ffn0"], w["ffn0_b"])
-        if geom.get("conv_plan") is not None:
+        if self.ffn_interleaved:
             y = fk.fast_sparse_conv3d_swiglu_planned(h2, w["conv_w"], w["conv_b"], geom["conv_plan"])
         else:
             y = fk.fast_sparse_conv3d(h2, w["conv_w"], w["conv_b"], geom["conv_indices"], fuse_swiglu=True)

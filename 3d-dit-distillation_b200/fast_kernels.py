@@ -231,8 +231,10 @@ def build_conv_plan(conv_indices, row_order: torch.Tensor) -> torch.Tensor:
 
 def fast_sparse_conv3d_swiglu_planned(feat: torch.Tensor, weight_fp32: torch.Tensor, bias_fp32: torch.Tensor,
                                       plan: torch.Tensor) -> torch.Tensor:
-    """silu(conv(feat)[:, C/2:]) * conv(feat)[:, :C/2], bit-identical to
-    ``fast_sparse_conv3d(..., fuse_swiglu=True)``, from a ``build_conv_plan``."""
+    """silu(conv(feat)[:, C/2:]) * conv(feat)[:, :C/2] from a ``build_conv_plan``, with
+    ``feat``, ``weight_fp32`` and ``bias_fp32`` in pair-interleaved column order
+    (a[2k], a[2k+1], gate[2k], gate[2k+1]); bit-identical to
+    ``fast_sparse_conv3d(..., fuse_swiglu=True)`` on the de-interleaved inputs."""
     n, c = feat.shape
     out = torch.empty(n, c // 2, dtype=BF16, device=feat.device)
     check(lib().vdit_dwconv27_swiglu_planned(ptr(feat), n, c, ptr(plan), ptr(weight_fp32), ptr(bias_fp32),

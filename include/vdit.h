@@ -145,9 +145,13 @@ int vdit_dwconv27(const void* h, int64_t n, int32_t c, const int32_t* idx, const
  * space-filling-curve order of the rows (row_order [n] int64, a permutation of
  * [0,n), e.g. the Hilbert fwd order of vdit_hilbert4_orders) into a caller-owned
  * buffer of vdit_dwconv27_plan_bytes(n) bytes, and depends on nothing else.
- * vdit_dwconv27_swiglu_planned gives bit-identical results to vdit_dwconv27
- * with fuse_swiglu=1 on the same idx; c must be a multiple of 128
- * (VDIT_ERR_UNSUPPORTED otherwise). */
+ * The input h [n,c] bf16, weights w [27,c] and bias b [c] fp32 are given in
+ * pair-interleaved column order: columns 4k..4k+3 hold (a[2k], a[2k+1],
+ * gate[2k], gate[2k+1]) where the reference packs [a | gate]; a caller gets h in
+ * this order by permuting the rows of the up-projection producing it.  out
+ * [n,c/2] bf16 is in natural channel order and bit-identical to vdit_dwconv27
+ * with fuse_swiglu=1 on the de-interleaved inputs.  c must be a multiple of 128
+ * (VDIT_ERR_UNSUPPORTED otherwise); h, w, b and plan 16-byte aligned. */
 size_t vdit_dwconv27_plan_bytes(int64_t n);
 int vdit_dwconv27_plan(const int32_t* idx, const int64_t* row_order, int64_t n, void* plan,
                        size_t plan_bytes, vdit_stream_t stream);

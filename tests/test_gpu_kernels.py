@@ -229,13 +229,20 @@ def test_dwconv27_swiglu_planned(case):
         vox, c = np.array([[3, 4, 5]], np.int32), 256
     h, w, b, idx, fwd = _planned_case(vox, c, 17)
     ref = fk.fast_sparse_conv3d(h, w, b, [idx], fuse_swiglu=True)
+    perm = _pair_interleave(c)
+    hp, wp, bp = h[:, perm].contiguous(), w[:, perm].contiguous(), b[perm].contiguous()
     for k in (0, 2):
         plan = fk.build_conv_plan([idx], fwd[k])
-        out = fk.fast_sparse_conv3d_swiglu_planned(h, w, b, plan)
+        out = fk.fast_sparse_conv3d_swiglu_planned(hp, wp, bp, plan)
         assert torch.equal(out, ref), (case, k, (out.float() - ref.float()).abs().max().item())
     # identity order: lexicographic blocks, mostly global-memory on the shell
     plan = fk.build_conv_plan([idx], torch.arange(h.shape[0], device=DEV))
-    assert torch.equal(fk.fast_sparse_conv3d_swiglu_planned(h, w, b, plan), ref)
+    assert torch.equal(fk.fast_sparse_conv3d_swiglu_planned(hp, wp, bp, plan), ref)
+
+
+def _pair_interleave(c):
+    """Column order (a[2k], a[2k+1], gate[2k], gate[2k+1]) of the staged conv's input."""
+    return torch.arange(c, device=DEV).view(2, c // 4, 2).permute(1, 0, 2).reshape(-1)
 
 
 def test_dwconv27_planned_vs_oracle():
@@ -244,7 +251,10 @@ def test_dwconv27_planned_vs_oracle():
     ref = om.dwconv27(h.float().cpu(), w.cpu(), b.cpu(), idx.cpu())
     a, gg = ref.chunk(2, -1)
     plan = fk.build_conv_plan([idx], fwd[0])
-    assert rel(fk.fast_sparse_conv3d_swiglu_planned(h, w, b, plan), torch.nn.functional.silu(gg) * a) < 1e-2
+    perm = _pair_interleave(768)
+    out = fk.fast_sparse_conv3d_swiglu_planned(h[:, perm].contiguous(), w[:, perm].contiguous(),
+                                               b[perm].contiguous(), plan)
+    assert rel(out, torch.nn.functional.silu(gg) * a) < 1e-2
 
 
 # ----------------------------------------------------------------------------- attention
