@@ -450,6 +450,7 @@ extern "C" int vdit_attention(const void* q, int64_t q_stride, const void* k, in
 namespace vdit {
 int dense_conv_error_word(int clear);   // error word of the dense conv kernel (dense_conv.cu)
 int dwconv_plan_error_word(int clear);  // error word of the staged depthwise conv (dwconv_plan.cu)
+int rowops_error_word(int clear);       // error word of the staged row kernels (rowops.cu)
 }
 
 extern "C" int vdit_device_error(int clear) {
@@ -464,5 +465,7 @@ extern "C" int vdit_device_error(int clear) {
     if (d < 0) return d;
     const int p = vdit::dwconv_plan_error_word(clear);
     if (p < 0) return p;
-    return v != 0 ? v : (d != 0 ? d : p);
+    const int r = vdit::rowops_error_word(clear);
+    if (r < 0) return r;
+    return v != 0 ? v : (d != 0 ? d : (p != 0 ? p : r));
 }

@@ -3,9 +3,15 @@
 // modulation + unpatchify, and the small sampler kernels.  All are HBM-bound:
 // rows move through registers/shared memory in 16-byte vectors, statistics
 // are reduced with warp shuffles in fp32.
+#include <algorithm>
+
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace vdit {
+
+__device__ int g_rowops_error = 0;
+
 namespace {
 
 constexpr int kRowWarps = 8;            // rows per 256-thread block
@@ -113,6 +119,125 @@ __global__ void __launch_bounds__(256) gate_add_modulate_kernel(
     float mean, rstd;
     row_stats(r, nvec, lane, d, mean, rstd);
     row_modulate_store(r, nvec, lane, mean, rstd, s1, sh, mod_out + row * d);
+}
+
+// The same operation as gate_add_modulate_kernel from persistent CTAs: one CTA
+// per SM stages g, s1, sh in shared memory once, and each warp walks rows with
+// a stride, bulk-copying the next row's x and h into its second buffer while
+// the current row is reduced and written.  Arithmetic is identical to the
+// one-row-per-warp kernel.  Waits on the bulk copies are bounded; a timeout
+// sets the row kernels' error word.
+constexpr int kGaMaxWarps = 16;
+constexpr int kErrRowTimeout = 0x524f;   // "RO": a bounded wait of a row kernel ran out
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(kGaMaxWarps * 32, 1) gate_add_modulate_staged_kernel(
+    __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ h, int64_t h_stride, int64_t m, int d,
+    const float* __restrict__ g, const float* __restrict__ s1, const float* __restrict__ sh,
+    __nv_bfloat16* __restrict__ mod_out) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int abort_flag;
+    const int nwarps = blockDim.x >> 5;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool mod = mod_out != nullptr;
+    float* pg = reinterpret_cast<float*>(smem);
+    float* ps1 = pg + d;
+    float* psh = ps1 + d;
+    const uint32_t row_bytes = 2u * (uint32_t)d;
+    uint8_t* wbuf = smem + (size_t)12 * d + (size_t)warp * 4 * row_bytes;   // [stage][x | h]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)12 * d + (size_t)nwarps * 4 * row_bytes) + warp * 2;
+    const uint32_t bar_u[2] = {tc::smem_u32(bars), tc::smem_u32(bars + 1)};
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        pg[i] = g[i];
+        if (mod) {
+            ps1[i] = s1[i];
+            psh[i] = sh[i];
+        }
+    }
+    if (threadIdx.x == 0) abort_flag = 0;
+    if (lane == 0) {
+        tc::mbar_init(bar_u[0], 1);
+        tc::mbar_init(bar_u[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    const int nvec = d >> 3;
+    const int64_t stride = (int64_t)gridDim.x * nwarps;
+    auto issue = [&](int64_t row, int b) {
+        const uint32_t dst = tc::smem_u32(wbuf + b * 2 * row_bytes);
+        tc::mbar_expect_tx(bar_u[b], 2 * row_bytes);
+        bulk_load(dst, x + row * d, row_bytes, bar_u[b]);
+        bulk_load(dst + row_bytes, h + row * h_stride, row_bytes, bar_u[b]);
+    };
+    int64_t row = (int64_t)blockIdx.x * nwarps + warp;
+    if (lane == 0 && row < m) issue(row, 0);
+    int it = 0;
+    bool ok = true;
+    for (; row < m; row += stride, ++it) {
+        const int b = it & 1;
+        if (lane == 0 && row + stride < m) issue(row + stride, b ^ 1);   // its buffer was read last row
+        ok = __all_sync(0xffffffffu, tc::mbar_wait(bar_u[b], (it >> 1) & 1, &abort_flag, &g_rowops_error,
+                                                   kErrRowTimeout));
+        if (!ok) break;
+        const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(wbuf + b * 2 * row_bytes);
+        const __nv_bfloat16* hs = xs + d;
+        __nv_bfloat16* xr = x + row * d;
+        RowRegs r;
+#pragma unroll
+        for (int i = 0; i < kMaxVec; ++i) {
+            const int vi = lane + 32 * i;
+            if (vi >= nvec) continue;
+            float xv[8], hv[8];
+            load8(xs + vi * 8, xv);
+            load8(hs + vi * 8, hv);
+            const float4 g0 = *reinterpret_cast<const float4*>(pg + vi * 8);
+            const float4 g1 = *reinterpret_cast<const float4*>(pg + vi * 8 + 4);
+            const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+            uint4 packed;
+            __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&packed);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                p2[j] = __floats2bfloat162_rn(xv[2 * j] + hv[2 * j] * gg[2 * j],
+                                              xv[2 * j + 1] + hv[2 * j + 1] * gg[2 * j + 1]);
+                const float2 t = __bfloat1622float2(p2[j]);
+                r.v[i][2 * j] = t.x;
+                r.v[i][2 * j + 1] = t.y;
+            }
+            *reinterpret_cast<uint4*>(xr + vi * 8) = packed;
+        }
+        __syncwarp();                                    // this buffer may be refilled after the next wait
+        if (!mod) continue;
+        float mean, rstd;
+        row_stats(r, nvec, lane, d, mean, rstd);
+        __nv_bfloat16* orow = mod_out + row * d;
+#pragma unroll
+        for (int i = 0; i < kMaxVec; ++i) {
+            const int vi = lane + 32 * i;
+            if (vi >= nvec) continue;
+            const float4 a0 = *reinterpret_cast<const float4*>(ps1 + vi * 8);
+            const float4 a1 = *reinterpret_cast<const float4*>(ps1 + vi * 8 + 4);
+            const float4 b0 = *reinterpret_cast<const float4*>(psh + vi * 8);
+            const float4 b1 = *reinterpret_cast<const float4*>(psh + vi * 8 + 4);
+            const float sa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float sb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+            float o[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = (r.v[i][j] - mean) * rstd * sa[j] + sb[j];
+            store8(orow + vi * 8, o);
+        }
+    }
+    if (lane == 0 && !ok) {
+        // a wait ran out: give the copies still in flight (rows it and it+1) time to land
+        volatile int no_abort = 0;
+        int ignored = 0;
+        for (int k = it; k < it + 2; ++k) tc::mbar_wait(bar_u[k & 1], (k >> 1) & 1, &no_abort, &ignored, 0);
+    }
 }
 
 // out[row, o] = sum_c bf16(LN(x)*s1+sh)[c] * w[o, c], 16 outputs, fp32
@@ -361,11 +486,53 @@ __global__ void unpermute_denorm_kernel(const float* __restrict__ xt, const int6
 inline unsigned blocks_for(int64_t n, int per) { return (unsigned)((n + per - 1) / per); }
 
 }  // namespace
+
+int rowops_error_word(int clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_rowops_error, sizeof(int)) != cudaSuccess) return VDIT_ERR_LAUNCH;
+    if (clear) {
+        int z = 0;
+        if (cudaMemcpyToSymbol(g_rowops_error, &z, sizeof(int)) != cudaSuccess) return VDIT_ERR_LAUNCH;
+    }
+    return v;
+}
+
 }  // namespace vdit
 
 using namespace vdit;
 
 static bool row_width_ok(int32_t d) { return d > 0 && d % 8 == 0 && d <= 256 * kMaxVec; }
+
+int launch_gate_add_staged(__nv_bfloat16* x, const __nv_bfloat16* h, int64_t h_stride, int64_t m, int d,
+                           const float* g, const float* s1, const float* sh, __nv_bfloat16* mod_out, cudaStream_t s) {
+    static int sms[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) {
+        if (e != cudaSuccess) record_cuda_error(e);
+        return VDIT_ERR_LAUNCH;
+    }
+    constexpr size_t kMaxSmem = 227 * 1024 - 256;
+    const size_t per_warp = (size_t)8 * d + 16;
+    const int nwarps = (int)std::min<size_t>(kGaMaxWarps, (kMaxSmem - (size_t)12 * d) / per_warp);
+    if (sms[dev] == 0) {
+        int n = 0;
+        e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gate_add_modulate_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kMaxSmem);
+        if (e != cudaSuccess) {
+            record_cuda_error(e);
+            return VDIT_ERR_LAUNCH;
+        }
+        sms[dev] = n;
+    }
+    const size_t smem = (size_t)12 * d + (size_t)nwarps * per_warp;
+    const unsigned grid = (unsigned)std::min<int64_t>((m + nwarps - 1) / nwarps, sms[dev]);
+    gate_add_modulate_staged_kernel<<<grid, nwarps * 32, smem, s>>>(x, h, h_stride, m, d, g, s1, sh, mod_out);
+    count_launches(1);
+    return check_launch();
+}
 
 extern "C" int vdit_patchify(const float* xt, int64_t n, const float* w, int32_t d, void* x_out, vdit_stream_t stream) {
     if (n < 0 || d <= 0 || d % 8 || !xt || !w || !x_out) return VDIT_ERR_ARG;
@@ -397,6 +564,10 @@ extern "C" int vdit_gate_add_modulate(void* x, const void* h, int64_t h_stride, 
         (s1 && !aligned16(s1)) || (sh && !aligned16(sh)))
         return VDIT_ERR_ALIGN;
     if (m == 0) return VDIT_OK;
+    if (m >= 4096)       // enough rows for persistent CTAs to pay off
+        return launch_gate_add_staged(static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(h), h_stride,
+                                      m, d, g, s1, sh, static_cast<__nv_bfloat16*>(mod_out),
+                                      static_cast<cudaStream_t>(stream));
     gate_add_modulate_kernel<<<blocks_for(m, kRowWarps), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(h), h_stride, m, d, g, s1, sh,
         static_cast<__nv_bfloat16*>(mod_out));

@@ -245,6 +245,30 @@ def qknorm_bench(w, reps: int = 20):
     return {"kernel": "qknorm_rope_kernel<0>", "ms_per_launch": ms, "gbs": byts / ms / 1e6}
 
 
+def gate_add_bench(w, reps: int = 20):
+    """Gate-add + LayerNorm + AdaLN modulation on the workload's shapes (N=16384, D=1536).
+    Algorithmic bytes: read x and h, write x and the modulated copy (4*N*D*2)."""
+    from vdit import fast_kernels as fk
+    D = w.arch.dim
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(w.n, D, device="cuda", generator=g).to(torch.bfloat16)
+    h = torch.randn(w.n, D, device="cuda", generator=g).to(torch.bfloat16)
+    gt, s1, sh = [torch.randn(D, device="cuda", generator=g) * 0.1 for _ in range(3)]
+    mod = torch.empty_like(x)
+    for _ in range(3):
+        fk.fast_gate_add_and_modulate(x, h, gt, s1, sh, out=mod)
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for _ in range(reps):
+        fk.fast_gate_add_and_modulate(x, h, gt, s1, sh, out=mod)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    return {"kernel": "gate_add_modulate", "ms_per_launch": ms, "gbs": 4 * w.n * D * 2 / ms / 1e6}
+
+
 def dense_conv_bench(reps: int = 5):
     """C3: dense 27-tap sparse conv, N=65536 voxels of a sphere shell (r=56) in 128^3,
     features [N,1536] bf16, weights [27,1536,1536], fp32 accumulation.  FLOPs are
@@ -284,7 +308,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="one warm-up sample, then one sample inside the NVTX range 'profile_step' (for ncu)")
-    ap.add_argument("--only", choices=["attention", "dwconv", "dense_conv", "qknorm"], default=None,
+    ap.add_argument("--only", choices=["attention", "dwconv", "dense_conv", "qknorm", "gate_add"], default=None,
                     help="run only one kernel on the workload's shapes (small ncu case)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -311,6 +335,9 @@ def main():
         return
     if args.only == "qknorm":
         print(json.dumps(qknorm_bench(w)))
+        return
+    if args.only == "gate_add":
+        print(json.dumps(gate_add_bench(w)))
         return
     if args.only == "dense_conv":
         print(json.dumps(dense_conv_bench()))

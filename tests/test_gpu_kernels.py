@@ -112,6 +112,25 @@ def test_modulate_and_gate_add(m, d):
     assert rel(x3, x.float() + h[0].float() * gt) < 5e-3
 
 
+@pytest.mark.parametrize("m,d,stride_h", [(4096, 1536, False), (9001, 1536, True), (5000, 768, False)])
+def test_gate_add_staged_matches_rowwise(m, d, stride_h):
+    """m >= 4096 rows take the persistent staged kernel; chunks below that the
+    one-row-per-warp kernel.  Both must produce identical bits."""
+    g = torch.Generator(device=DEV).manual_seed(m)
+    x = torch.randn(m, d, device=DEV, generator=g).to(torch.bfloat16)
+    hs = torch.randn(m, 2 * d if stride_h else d, device=DEV, generator=g).to(torch.bfloat16)
+    h = hs[:, d:] if stride_h else hs                   # a row stride of 2d
+    s1, sh, gt = [torch.randn(d, device=DEV, generator=g) * 0.3 + o for o in (1.0, 0.0, 0.0)]
+    xa = x.clone()
+    mod_a = fk.fast_gate_add_and_modulate(xa, h, gt, s1, sh)
+    xb = x.clone()
+    mods = [fk.fast_gate_add_and_modulate(xb[i:i + 2048], h[i:i + 2048], gt, s1, sh) for i in range(0, m, 2048)]
+    assert torch.equal(xa, xb) and torch.equal(mod_a, torch.cat(mods))
+    xc = x.clone()
+    fk.fast_gate_add_and_modulate(xc, h, gt, None, None)
+    assert torch.equal(xc, xa)
+
+
 def test_out_modulate_unpatchify():
     g = torch.Generator(device=DEV).manual_seed(3)
     x = torch.randn(777, 1536, device=DEV, generator=g).to(torch.bfloat16)
