@@ -1,14 +1,18 @@
 // Dense 27-tap submanifold sparse conv on tcgen05 tensor cores (implicit GEMM):
 //   out[n, co] = b[co] + sum_d sum_ci W[d, co, ci] * f[idx[n, d], ci]
-// M = voxels (128-row tiles), N = output channels (256 per CTA, one TMEM
-// accumulator of 256 fp32 columns), K = taps x input channels (64 per step).
-// Warps 0..3 gather the A tile rows f[idx[n,d], k0:k0+64] with cp.async
-// (16-byte copies into the 128B-swizzled K-major layout the MMA reads; absent
-// neighbours copy zero bytes and read as zeros), warp 4 loads the weight tile
-// W[d, co0:co0+256, k0:k0+64] with TMA (128B swizzle), warp 5 issues the MMAs.
-// A 4-stage ring overlaps gathers, weight loads and MMAs.  Taps that no row of
-// the tile has are skipped.  Warps 0..3 then drain TMEM, add the bias and store
-// bf16.  All mbarrier waits are bounded (error word + CTA abort flag).
+// M = voxels (two 128-row tiles per CTA sharing every weight tile), N = output
+// channels (256 per CTA; one TMEM accumulator of 256 fp32 columns per M tile,
+// 512 columns in all), K = taps x input channels (64 per step).  Sharing the
+// weight tile between 256 rows halves the weight stream from L2, which bounds
+// the one-tile form.
+// Warps 0..7 gather the A rows f[idx[n,d], k0:k0+64] with cp.async (eight
+// lanes per row, 16-byte copies into the 128B-swizzled K-major layout the MMA reads;
+// absent neighbours copy zero bytes and read as zeros), warp 8 loads the weight
+// tile W[d, co0:co0+256, k0:k0+64] with TMA (128B swizzle), warp 9 issues the
+// MMAs.  A 3-stage ring overlaps gathers, weight loads and MMAs.  Taps that no
+// row of the CTA has are skipped.  Warps 0..7 then drain TMEM (warp w: tile
+// w/4, lane quarter w%4), add the bias and store bf16.  All mbarrier waits are
+// bounded (error word + CTA abort flag).
 #include <string.h>
 
 #include "common.cuh"
@@ -22,14 +26,15 @@ namespace dconv {
 
 using namespace tc;
 
-constexpr int BM = 128, BN = 256, BK = 64, S = 4;
-constexpr int THREADS = 192;
+constexpr int BM = 128, MT = 2, ROWS = BM * MT, BN = 256, BK = 64, S = 3;
+constexpr int GATHER_WARPS = ROWS / 32;               // 8
+constexpr int THREADS = (GATHER_WARPS + 2) * 32;      // + TMA warp + MMA warp
 constexpr int kErr = 0x4443;   // "DC": a bounded wait of the dense conv kernel ran out
 
 struct __align__(1024) Smem {
-    uint8_t a[S][BM * 128];
+    uint8_t a[S][MT][BM * 128];
     uint8_t b[S][BN * 128];
-    int32_t idx[BM * 27];
+    int32_t idx[ROWS * 27];
     uint64_t full_a[S], full_b[S], empty[S], acc_full;
     uint32_t tmem_slot;
     int abort_flag;
@@ -66,27 +71,27 @@ __global__ void __launch_bounds__(THREADS, 1) dense_conv27_kernel(const __grid_c
     extern __shared__ uint8_t raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t row0 = (int64_t)blockIdx.x * BM;
+    const int64_t row0 = (int64_t)blockIdx.x * ROWS;
     const int co0 = blockIdx.y * BN;
-    const int nrows = (int)min((int64_t)BM, n - row0);
+    const int nrows = (int)min((int64_t)ROWS, n - row0);
     volatile int* abort_flag = &sm.abort_flag;
 
     if (tid == 0) {
         sm.tapmask = 0;
         sm.abort_flag = 0;
     }
-    for (int t = tid; t < BM * 27; t += THREADS) sm.idx[t] = (t < nrows * 27) ? __ldg(idx + row0 * 27 + t) : -1;
+    for (int t = tid; t < ROWS * 27; t += THREADS) sm.idx[t] = (t < nrows * 27) ? __ldg(idx + row0 * 27 + t) : -1;
     __syncthreads();
     {
         unsigned m = 0;
-        for (int t = tid; t < BM * 27; t += THREADS)
+        for (int t = tid; t < ROWS * 27; t += THREADS)
             if (sm.idx[t] >= 0) m |= 1u << (t % 27);
         m = __reduce_or_sync(0xffffffffu, m);
         if (lane == 0) atomicOr(&sm.tapmask, m);
     }
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(smem_u32(&sm.full_a[s]), 128);
+            mbar_init(smem_u32(&sm.full_a[s]), ROWS);
             mbar_init(smem_u32(&sm.full_b[s]), 1);
             mbar_init(smem_u32(&sm.empty[s]), 1);
         }
@@ -94,8 +99,8 @@ __global__ void __launch_bounds__(THREADS, 1) dense_conv27_kernel(const __grid_c
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
     }
-    if (warp == 5) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(&sm.tmem_slot)));
+    if (warp == GATHER_WARPS + 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&sm.tmem_slot)));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
         tc_fence_before();
     }
@@ -106,9 +111,14 @@ __global__ void __launch_bounds__(THREADS, 1) dense_conv27_kernel(const __grid_c
     const int nkc = cin / BK;
     const int n_iter = __popc(mask) * nkc;
 
-    if (warp < 4) {
-        // ------------------------------------------------------------ A gather (row r = tid)
-        const int r = tid;
+    if (warp < GATHER_WARPS) {
+        // ------------------------------------------------------------ A gather
+        // thread t copies 16-byte chunk t%8 of rows t/8 + 32k (k = 0..7): the eight lanes of
+        // a group cover one row's 128 contiguous bytes, so a warp instruction moves four
+        // whole rows and no 32-byte sector is fetched twice
+        const int r = tid;                                 // the row this thread drains later
+        const int mt = r / BM;
+        const int ch = tid & 7, rb = tid >> 3;
         TapWalk tw;
         tw.init(mask, nkc);
         int i = 0;
@@ -116,12 +126,13 @@ __global__ void __launch_bounds__(THREADS, 1) dense_conv27_kernel(const __grid_c
             const int s = i % S;
             if (i >= S && !mbar_wait(smem_u32(&sm.empty[s]), ((i / S) - 1) & 1, abort_flag, &g_dense_error, kErr))
                 break;
-            const int src = sm.idx[r * 27 + tw.tap];
-            const __nv_bfloat16* p = f + (int64_t)(src >= 0 ? src : 0) * cin + tw.kc * BK;
-            const uint32_t dst = smem_u32(sm.a[s]) + r * 128;
-            const uint32_t bytes = src >= 0 ? 16u : 0u;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) cp_async16(dst + ((c ^ (r & 7)) << 4), p + c * 8, bytes);
+            for (int k = 0; k < ROWS / 32; ++k) {
+                const int rr = rb + 32 * k, rt = rr % BM;
+                const int src = sm.idx[rr * 27 + tw.tap];
+                const __nv_bfloat16* p = f + (int64_t)(src >= 0 ? src : 0) * cin + tw.kc * BK + ch * 8;
+                cp_async16(smem_u32(sm.a[s][rr / BM]) + rt * 128 + ((ch ^ (rt & 7)) << 4), p, src >= 0 ? 16u : 0u);
+            }
             asm volatile("cp.async.commit_group;" ::: "memory");
             if (i >= S - 1) {
                 asm volatile("cp.async.wait_group %0;" ::"n"(S - 1) : "memory");
@@ -137,7 +148,8 @@ __global__ void __launch_bounds__(THREADS, 1) dense_conv27_kernel(const __grid_c
                                                     mbar_wait(smem_u32(&sm.acc_full), 0, abort_flag, &g_dense_error, kErr));
         if (ok) {
             tc_fence_after();
-            const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
+            // warp w reads the TMEM lane quarter w%4 of tile w/4: its rows are exactly r
+            const uint32_t taddr = tmem + mt * BN + ((uint32_t)((warp & 3) * 32) << 16);
             const bool live = r < nrows;
             __nv_bfloat16* dst = out + (row0 + r) * cout + co0;
 #pragma unroll 1
@@ -153,7 +165,7 @@ __global__ void __launch_bounds__(THREADS, 1) dense_conv27_kernel(const __grid_c
                 }
             }
         }
-    } else if (warp == 4) {
+    } else if (warp == GATHER_WARPS) {
         // ------------------------------------------------------------ weight tiles (TMA)
         if (lane == 0) {
             TapWalk tw;
@@ -179,11 +191,15 @@ __global__ void __launch_bounds__(THREADS, 1) dense_conv27_kernel(const __grid_c
                     break;
                 }
                 tc_fence_after();
-                const uint32_t abase = smem_u32(sm.a[s]), bbase = smem_u32(sm.b[s]);
+                const uint32_t bbase = smem_u32(sm.b[s]);
 #pragma unroll
-                for (int kk = 0; kk < BK / 16; ++kk)
-                    tc_mma(tmem, make_desc(abase + kk * 32, 16, 1024, kSw128), make_desc(bbase + kk * 32, 16, 1024, kSw128),
-                           IDESC, (i > 0 || kk > 0) ? 1u : 0u);
+                for (int t = 0; t < MT; ++t) {
+                    const uint32_t abase = smem_u32(sm.a[s][t]);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        tc_mma(tmem + t * BN, make_desc(abase + kk * 32, 16, 1024, kSw128),
+                               make_desc(bbase + kk * 32, 16, 1024, kSw128), IDESC, (i > 0 || kk > 0) ? 1u : 0u);
+                }
                 tc_commit(smem_u32(&sm.empty[s]));
             }
             if (ok) tc_commit(smem_u32(&sm.acc_full));
@@ -192,9 +208,9 @@ __global__ void __launch_bounds__(THREADS, 1) dense_conv27_kernel(const __grid_c
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == GATHER_WARPS + 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
     }
 }
 
@@ -242,7 +258,7 @@ extern "C" int vdit_dense_conv27(const void* f, int64_t n, int32_t cin, int32_t 
         }
         configured = true;
     }
-    dim3 grid((unsigned)((n + BM - 1) / BM), (unsigned)(cout / BN));
+    dim3 grid((unsigned)((n + ROWS - 1) / ROWS), (unsigned)(cout / BN));
     dense_conv27_kernel<<<grid, THREADS, sm, static_cast<cudaStream_t>(stream)>>>(
         m, static_cast<const __nv_bfloat16*>(f), n, cin, cout, idx, b, static_cast<__nv_bfloat16*>(out));
     count_launches(1);
