@@ -19,6 +19,8 @@ over the N voxels.
 from __future__ import annotations
 
 import math
+from collections import OrderedDict
+from dataclasses import dataclass
 from pathlib import Path
 from typing import Any, Dict, List, Optional
 
@@ -41,11 +43,34 @@ def _time_encoding(t: torch.Tensor, dim: int, max_period: float = 10000.0) -> to
     return torch.cat([torch.cos(f), torch.sin(f)], -1).float()
 
 
+@dataclass
+class _SampleGraph:
+    """A captured sample: the graph and the buffers it reads and writes."""
+    graph: "torch.cuda.CUDAGraph"
+    geom: Dict[str, Any]
+    context: torch.Tensor
+    noise: torch.Tensor
+    out: torch.Tensor
+
+
+def _copy_into(dst, src) -> None:
+    """Copy every tensor of a geometry dict (nested lists/tuples) into its counterpart."""
+    if torch.is_tensor(dst):
+        if dst is not src:
+            dst.copy_(src)
+    elif isinstance(dst, dict):
+        for k, v in dst.items():
+            _copy_into(v, src[k])
+    elif isinstance(dst, (list, tuple)):
+        for a, b in zip(dst, src):
+            _copy_into(a, b)
+
+
 class OptimizedLatDitRunner:
     """Runs ``FlowModel`` NFEs and the exact sampler on one CUDA device."""
 
     def __init__(self, model, solver_config: Optional[SolverConfig] = None, weights_dir: Optional[Path] = None,
-                 device: Optional[torch.device] = None):
+                 device: Optional[torch.device] = None, cuda_graph: bool = False):
         if hasattr(model, "core") and not isinstance(model, LatDitModel):   # a reference LatDitModel
             core = model.core
             mc = dict(core.model_config, latent_scale=float(core.latent_scale))
@@ -64,6 +89,10 @@ class OptimizedLatDitRunner:
         self._time_gates_cache: Dict[float, Dict[str, torch.Tensor]] = {}
         self._rope_2d_cache: Dict[int, tuple] = {}
         self._b0_share = None
+        # CUDA-graph replay of the sampler (per voxel count, context length and schedule)
+        self.cuda_graph = bool(cuda_graph)
+        self._graphs: "OrderedDict[tuple, _SampleGraph]" = OrderedDict()
+        self.max_graphs = 4
         self._prepare_weights_and_buffers()
 
     # ------------------------------------------------------------------ weights
@@ -372,13 +401,18 @@ class OptimizedLatDitRunner:
     def sample_with_context(self, vox: torch.Tensor, context: torch.Tensor, *,
                             sampling: Optional[FlowMatchSamplingParams] = None,
                             generator: Optional[torch.Generator] = None,
-                            noise: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """The sampler on one sample with the image context already mapped ([L, D])."""
+                            noise: Optional[torch.Tensor] = None,
+                            cuda_graph: Optional[bool] = None) -> torch.Tensor:
+        """The sampler on one sample with the image context already mapped ([L, D]).
+        With ``cuda_graph`` (default: the runner's setting) the GPU part of the sample
+        (noise gather, all NFEs, CFG + Euler, un-permutation) is captured once per
+        (voxel count, context length, schedule) and replayed; the geometry is built
+        eagerly for every sample and copied into the captured buffers."""
         geom = self._prepare_sample_geometry([vox], context)
         N = geom["N"]
         if noise is None:
             noise = torch.randn(N, self.latent_dim, dtype=F32, device=self.device, generator=generator)
-        xt = fk.gather_rows_f32(noise.to(self.device), geom["perm"])
+        noise = noise.to(self.device, F32)
         sc = self.solver_config
         g_scale, steps_ovr, r_ovr, cr_ovr = sc.guidance_scale, None, None, None
         if sampling is not None:
@@ -388,7 +422,27 @@ class OptimizedLatDitRunner:
             if sampling.num_inference_steps != 50:
                 steps_ovr = int(sampling.num_inference_steps)
         t_seq, guided, _ = build_schedule(sc, steps_ovr, r_ovr, cr_ovr)
-        tl = t_seq.tolist()
+        tl = [float(t) for t in t_seq.tolist()]
+        guided = [bool(g) for g in guided]
+        use_graph = self.cuda_graph if cuda_graph is None else bool(cuda_graph)
+        if not use_graph:
+            return self._sample_steps(geom, context, noise, tl, guided, g_scale)
+        key = (N, int(context.shape[-2]), tuple(tl), tuple(guided), g_scale)
+        entry = self._graphs.get(key)
+        if entry is None:
+            entry = self._capture_sample(key, geom, context, noise, tl, guided, g_scale)
+        else:
+            self._graphs.move_to_end(key)
+            _copy_into(entry.geom, geom)
+            entry.context.copy_(context)
+            entry.noise.copy_(noise)
+        entry.graph.replay()
+        return entry.out.clone()
+
+    def _sample_steps(self, geom: Dict[str, Any], context: torch.Tensor, noise: torch.Tensor, tl: List[float],
+                      guided: List[bool], g_scale: float) -> torch.Tensor:
+        """GPU part of the sampler: Euler + CFG over the schedule, latents in input order."""
+        xt = fk.gather_rows_f32(noise, geom["perm"])
         for i in range(len(guided)):
             v = self.forward_flow_fast(xt, tl[i], context, None, geom)
             vn = None
@@ -397,6 +451,25 @@ class OptimizedLatDitRunner:
             fk.cfg_euler_(xt, v, vn, g_scale, tl[i] - tl[i + 1])
         self._b0_share = None
         return fk.unpermute_denorm(xt, geom["up_widx"], self._denorm_scale, self._denorm_shift)
+
+    def _capture_sample(self, key, geom, context, noise, tl, guided, g_scale) -> "_SampleGraph":
+        """Run the sample once eagerly on a side stream (first-call set-up of every kernel,
+        time gates cached), then capture it on the static buffers."""
+        ctx = context.clone()
+        nz = noise.clone()
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self._sample_steps(geom, ctx, nz, tl, guided, g_scale)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = self._sample_steps(geom, ctx, nz, tl, guided, g_scale)
+        entry = _SampleGraph(graph, geom, ctx, nz, out)
+        self._graphs[key] = entry
+        while len(self._graphs) > self.max_graphs:
+            self._graphs.popitem(last=False)
+        return entry
 
     @torch.no_grad()
     def warmup(self) -> None:

@@ -50,14 +50,15 @@ class Solution(LatDitGenerator):
     """B200 lat_dit generator: exact Euler+CFG sampler with the 1-token uncond branch."""
 
     def __init__(self, inner: LatDitModel, solver_config: Optional[SolverConfig] = None,
-                 weights_dir: Optional[Path] = None, device: Optional[torch.device] = None):
+                 weights_dir: Optional[Path] = None, device: Optional[torch.device] = None,
+                 cuda_graph: bool = False):
         self.inner = inner
         self.solver_config = solver_config or SolverConfig()
         sc = self.solver_config
         self._default_runtime = FlowMatchSamplingParams(guidance_scale=sc.guidance_scale, cfg_range=sc.cfg_range,
                                                         rescale_t=sc.rescale_t,
                                                         num_inference_steps=sc.num_inference_steps)
-        self.runner = OptimizedLatDitRunner(inner, sc, weights_dir=weights_dir, device=device)
+        self.runner = OptimizedLatDitRunner(inner, sc, weights_dir=weights_dir, device=device, cuda_graph=cuda_graph)
 
     @classmethod
     def from_pretrained(cls, pretrained_model_name_or_path: Union[str, os.PathLike],
@@ -76,7 +77,8 @@ class Solution(LatDitGenerator):
         solver = SolverConfig.from_dir(primary, fallback_model_cfg=mc)
         if device is not None:
             device = torch.device(f"cuda:{device}" if isinstance(device, int) else device)
-        inst = cls(model, solver_config=solver, weights_dir=primary, device=device)
+        inst = cls(model, solver_config=solver, weights_dir=primary, device=device,
+                   cuda_graph=bool(kwargs.get("cuda_graph", False)))
         if solver.warmup_on_load:
             inst.runner.warmup()
         return inst
@@ -88,7 +90,7 @@ class Solution(LatDitGenerator):
         dev = kwargs.get("device", args[0] if args else None)
         if dev is not None:
             self.runner = OptimizedLatDitRunner(self.inner, self.solver_config, self.runner.weights_dir,
-                                                device=torch.device(dev))
+                                                device=torch.device(dev), cuda_graph=self.runner.cuda_graph)
         return self
 
     def eval(self) -> "Solution":

@@ -299,6 +299,42 @@ def dense_conv_bench(reps: int = 5):
             "tflops_nnz": 2.0 * nnz * cin * cout / ms / 1e9, "tflops_dense27": 2.0 * 27 * n * cin * cout / ms / 1e9}
 
 
+def graph_bench(w, reps: int = 5):
+    """Sample latency, eager vs CUDA-graph replay, on the workload's model at N = 4632
+    (the size of the smallest public-test voxel set) and at the workload's N."""
+    from vdit.fast_flow import OptimizedLatDitRunner
+    from vdit.fast_sampler import SolverConfig
+    from vdit.model import LatDitModel
+    from vdit.runtime import LatDitConditioning
+    from vdit.workloads import shell_voxels
+    dev = torch.device("cuda", torch.cuda.current_device())
+    model = LatDitModel.random(w.arch, seed=0, device=dev)
+    solver = SolverConfig(num_inference_steps=4, n_guided_steps=3, n_unguided_steps=1, guidance_scale=w.guidance)
+    runner = OptimizedLatDitRunner(model, solver, device=dev)
+    g = torch.Generator().manual_seed(9)
+    dino = torch.randn(1, w.ctx_tokens, w.arch.dino_dim, generator=g).to(dev, torch.float16)
+    cond = LatDitConditioning(dino_features=dino)
+    out = {"kernel": "sample (7 NFE)", "reps": reps}
+    for n, radius in ((4632, 30.0), (w.n, w.radius)):
+        vox = torch.from_numpy(shell_voxels(n, w.grid, radius, 1)).to(dev)
+        noise = torch.randn(len(vox), 16, generator=g).to(dev)
+        res = {}
+        for mode in (False, True):
+            runner.cuda_graph = mode
+            for _ in range(2):
+                runner.sample_fast([vox], cond, noise=noise)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                runner.sample_fast([vox], cond, noise=noise)
+            e1.record()
+            torch.cuda.synchronize()
+            res["graph_ms" if mode else "eager_ms"] = e0.elapsed_time(e1) / reps
+        out[f"n{len(vox)}"] = res
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -308,7 +344,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="one warm-up sample, then one sample inside the NVTX range 'profile_step' (for ncu)")
-    ap.add_argument("--only", choices=["attention", "dwconv", "dense_conv", "qknorm", "gate_add"], default=None,
+    ap.add_argument("--only", choices=["attention", "dwconv", "dense_conv", "qknorm", "gate_add", "graph"], default=None,
                     help="run only one kernel on the workload's shapes (small ncu case)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -338,6 +374,9 @@ def main():
         return
     if args.only == "gate_add":
         print(json.dumps(gate_add_bench(w)))
+        return
+    if args.only == "graph":
+        print(json.dumps(graph_bench(w)))
         return
     if args.only == "dense_conv":
         print(json.dumps(dense_conv_bench()))

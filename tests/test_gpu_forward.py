@@ -75,3 +75,25 @@ def test_sampler_matches_oracle():
     assert lat.shape == (len(vox), 16) and lat.dtype == torch.float32
     assert rel(lat, lat_o) < 2e-2
     assert _lib.device_error() == 0
+
+
+def test_graph_replay_matches_eager():
+    """The CUDA-graph sampler equals the eager one on the sample it was captured with
+    and on another sample of the same size (new voxels, context and noise copied in)."""
+    cfg, p, runner, vox, ctx_unused, _ = build(512, 128, depth=2, cdepth=1, n=700, side=8, patch=256, seed=7)
+    g = torch.Generator().manual_seed(8)
+    cases = []
+    for seed in (11, 12):
+        v = shell_voxels(700, 64, 22.0, seed)
+        assert len(v) == 700
+        dino = torch.randn(1, 5 + 64, 1280, generator=g).to(DEV)
+        cases.append((torch.from_numpy(v).to(DEV), LatDitConditioning(dino_features=dino),
+                      torch.randn(700, 16, generator=g).to(DEV)))
+    for v, cond, noise in cases:
+        eager = runner.sample_fast([v], cond, noise=noise)[0]
+        runner.cuda_graph = True
+        graphed = runner.sample_fast([v], cond, noise=noise)[0]
+        runner.cuda_graph = False
+        assert rel(graphed, eager) < 1e-4
+    assert len(runner._graphs) == 1
+    assert _lib.device_error() == 0
