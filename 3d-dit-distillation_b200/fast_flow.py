@@ -89,6 +89,9 @@ class OptimizedLatDitRunner:
         self._time_gates_cache: Dict[float, Dict[str, torch.Tensor]] = {}
         self._rope_2d_cache: Dict[int, tuple] = {}
         self._b0_share = None
+        # when a list, every window self-attention launch appends (start event, end event,
+        # window sizes) to it -- the benchmark's in-step measurement of that kernel
+        self.attention_timer: Optional[list] = None
         # CUDA-graph replay of the sampler (per voxel count, context length and schedule)
         self.cuda_graph = bool(cuda_graph)
         self._graphs: "OrderedDict[tuple, _SampleGraph]" = OrderedDict()
@@ -246,7 +249,15 @@ class OptimizedLatDitRunner:
         fwd, _bwd, cu, _ = geom["order_caches"][b % len(geom["order_caches"])]
         qkv_s = fk.fused_qknorm_rope3d_gather(qkv, w["qs"], w["ks"], self.cos3, self.sin3, geom["h_coords"], fwd, H,
                                               HD)
+        timer = self.attention_timer
+        if timer is not None:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record()
         o = fk.attention(qkv_s[:, :D], qkv_s[:, D:2 * D], qkv_s[:, 2 * D:], cu.host, cu.host, H, HD, out_rows=fwd)
+        if timer is not None:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+            timer.append((e0, e1, [cu.host[i + 1] - cu.host[i] for i in range(len(cu.host) - 1)]))
         return F.linear(o, w["to_out"], w["to_out_b"])
 
     def _ffn(self, b: int, h_mod: torch.Tensor, geom) -> torch.Tensor:

@@ -47,6 +47,14 @@ def _peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def _peaks_sustained() -> float:
+    """bf16 GEMM rate held for seconds under the power cap (for a kernel timed inside a long step)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()).get("bf16_tflops_sustained", 1400.0)
+    return 1400.0
+
+
 class ClockSampler:
     """nvidia-smi clock / throttle samples every 200 ms during the timed region."""
 
@@ -417,6 +425,8 @@ def main():
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
+    att_events: list = []
+    runner.attention_timer = att_events          # window self-attention launches inside the timed steps
     with ClockSampler(local) as clk:
         for i in range(args.steps):
             _l2_flush(flush)
@@ -424,6 +434,7 @@ def main():
             step()
             evs[i][1].record(s)
         torch.cuda.synchronize()
+    runner.attention_timer = None
     launches = (_lib.launch_count() - launches0) // max(args.steps, 1)
     total_ms = sum(a.elapsed_time(b) for a, b in evs)
     t = torch.tensor([total_ms], device=dev)
@@ -481,8 +492,13 @@ def main():
 
     # ---------------------------------------------------------------- roofline of the attention kernel
     hbm, tflops_peak, peak_kind = _peaks()
-    flops, att_ms = attention_roofline(w, runner)
-    achieved = flops / (att_ms / 1e3) / 1e12
+    tflops_sustained = _peaks_sustained()
+    # live: average duration of the window self-attention launches inside the timed steps
+    # (CUDA events on their stream), against the sustained GEMM peak
+    live_ms = statistics.fmean(a.elapsed_time(b) for a, b, _ in att_events)
+    flops = statistics.fmean(sum(4.0 * n * n * w.arch.dim for n in sizes) for _, _, sizes in att_events)
+    achieved = flops / (live_ms / 1e3) / 1e12
+    flops_alone, att_ms_alone = attention_roofline(w, runner)
     traffic = None
     tp = ROOT / "profiles" / "fmha_traffic.json"
     if tp.exists():
@@ -513,9 +529,15 @@ def main():
                     "api": "Solution.generate (pinned host voxels + fp16 DINO in, latents to host)"},
             "gpu_launches": int(launches),
             "roofline": {"kernel": "fmha_fwd_kernel<128> (window self-attention, 4x4096 voxels, 12x128)",
-                         "bound": "tensor", "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s",
-                         "frac": achieved / tflops_peak, "peak_kind": f"{peak_kind} burst bf16",
-                         "flops_per_launch": flops, "ms_per_launch": att_ms, "traffic": traffic},
+                         "bound": "tensor", "achieved": achieved, "peak": tflops_sustained, "unit": "TFLOP/s",
+                         "frac": achieved / tflops_sustained,
+                         "peak_kind": f"{peak_kind} sustained bf16 (kernel timed inside the timed steps)",
+                         "flops_per_launch": flops, "ms_per_launch": live_ms, "launches": len(att_events),
+                         "traffic": traffic,
+                         "alone": {"ms_per_launch": att_ms_alone,
+                                   "achieved": flops_alone / (att_ms_alone / 1e3) / 1e12,
+                                   "peak": tflops_peak, "peak_kind": f"{peak_kind} burst bf16",
+                                   "frac": flops_alone / (att_ms_alone / 1e3) / 1e12 / tflops_peak}},
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
         }), flush=True)
