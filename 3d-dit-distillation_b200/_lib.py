@@ -37,6 +37,8 @@ SIGNATURES = {
     "vdit_qknorm_rope3d_gather": (ctypes.c_int, [_vp, _c_i64, _c_i32, _c_i32, _vp, _vp, _vp, _vp, _c_i32, _vp,
                                                  _vp, _vp, _vp]),
     "vdit_qknorm_rope2d": (ctypes.c_int, [_vp, _c_i64, _c_i32, _c_i32, _vp, _vp, _vp, _vp, _c_i32, _vp]),
+    "vdit_vec_ln_modulate": (ctypes.c_int, [_vp, _c_i32, _vp, _vp, _vp, _vp]),
+    "vdit_vec_gate_residual": (ctypes.c_int, [_vp, _vp, _vp, _c_i32, _vp]),
     "vdit_swiglu_packed": (ctypes.c_int, [_vp, _c_i64, _c_i32, _vp, _vp]),
     "vdit_dwconv27": (ctypes.c_int, [_vp, _c_i64, _c_i32, _vp, _vp, _vp, _vp, _c_i32, _vp]),
     "vdit_dwconv27_plan_bytes": (ctypes.c_size_t, [_c_i64]),

@@ -405,6 +405,53 @@ __global__ void __launch_bounds__(kQkWarps * 32) qknorm_rope_kernel(
     }
 }
 
+// ---------------------------------------------------------------- context vector (1-token branch)
+// out = bf16(LN(v) * s1 + sh) for one fp32 vector (d <= 2048): one block, two-pass
+// statistics (mean, then mean of squared deviations) in fp32.
+__global__ void __launch_bounds__(256) vec_ln_modulate_kernel(const float* __restrict__ v, int d,
+                                                              const float* __restrict__ s1,
+                                                              const float* __restrict__ sh,
+                                                              __nv_bfloat16* __restrict__ out) {
+    __shared__ float red[8];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float x[8];
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int i = tid + 256 * k;
+        x[k] = i < d ? v[i] : 0.f;
+        s += x[k];
+    }
+    auto block_sum = [&](float t) {
+        t = warp_sum(t);
+        __syncthreads();
+        if (lane == 0) red[warp] = t;
+        __syncthreads();
+        float r = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) r += red[w];
+        return r;
+    };
+    const float mean = block_sum(s) / (float)d;
+    float q = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+        if (tid + 256 * k < d) q += (x[k] - mean) * (x[k] - mean);
+    const float rstd = rsqrtf(block_sum(q) / (float)d + 1e-6f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int i = tid + 256 * k;
+        if (i < d) out[i] = f2bf((x[k] - mean) * rstd * s1[i] + sh[i]);
+    }
+}
+
+// c += float(y) * g for one fp32 vector and a bf16 update
+__global__ void vec_gate_residual_kernel(float* __restrict__ c, const __nv_bfloat16* __restrict__ y,
+                                         const float* __restrict__ g, int d) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < d) c[i] += bf2f(y[i]) * g[i];
+}
+
 // ---------------------------------------------------------------- misc
 __global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ h, int64_t m, int f, __nv_bfloat16* __restrict__ out) {
     int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -613,6 +660,24 @@ extern "C" int vdit_qknorm_rope2d(void* qkv, int64_t l, int32_t heads, int32_t h
     qknorm_rope_kernel<1><<<blocks_for(l, kQkWarps), kQkWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(qkv), l, heads, hd, qs, ks, cs, sn, 1,
         nullptr, nullptr, n_prefix);
+    count_launches(1);
+    return check_launch();
+}
+
+extern "C" int vdit_vec_ln_modulate(const float* v, int32_t d, const float* s1, const float* sh, void* out,
+                                    vdit_stream_t stream) {
+    if (d <= 0 || !v || !s1 || !sh || !out) return VDIT_ERR_ARG;
+    if (d > 2048) return VDIT_ERR_UNSUPPORTED;
+    vec_ln_modulate_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(v, d, s1, sh,
+                                                                            static_cast<__nv_bfloat16*>(out));
+    count_launches(1);
+    return check_launch();
+}
+
+extern "C" int vdit_vec_gate_residual(float* c, const void* y, const float* g, int32_t d, vdit_stream_t stream) {
+    if (d <= 0 || !c || !y || !g) return VDIT_ERR_ARG;
+    vec_gate_residual_kernel<<<(d + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        c, static_cast<const __nv_bfloat16*>(y), g, d);
     count_launches(1);
     return check_launch();
 }

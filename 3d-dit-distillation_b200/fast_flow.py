@@ -344,12 +344,9 @@ class OptimizedLatDitRunner:
                                    and self._b0_share[1].shape[0] == xt_sorted.shape[0]) else None
         c = torch.zeros(D, dtype=F32, device=xt_sorted.device)
 
-        def ln(v):
-            mu = v.mean()
-            return (v - mu) * torch.rsqrt(((v - mu) ** 2).mean() + 1e-6)
-
-        def lin(v, wk, bk, blk):
-            return F.linear(v.to(BF16), blk[wk], blk[bk]).float()
+        def mod_lin(scale1, shift, wk, bk, blk):
+            """bf16 Linear(LN(c) * scale1 + shift) of the context vector."""
+            return F.linear(fk.vec_ln_modulate(c, scale1, shift), blk[wk], blk[bk])
 
         if share is not None:
             x = share[1].clone()
@@ -359,7 +356,6 @@ class OptimizedLatDitRunner:
             x = fk.patchify(xt_sorted, self.W_patch)
             h_mod = fk.fast_modulate(x, None, G[0, 0], G[0, 1])
             start = 0
-        ln_c = None
         for b in range(self.depth):
             w = self.blocks[b]
             if b >= start:
@@ -367,24 +363,21 @@ class OptimizedLatDitRunner:
                 h_mod = fk.fast_gate_add_and_modulate(x, h, G[b, 2], G[b, 3], G[b, 4])
             if b < cd:
                 CG = CG9[b]
-                c = c + lin(ln(c) * CG[0] + CG[1], "msa1_w", "msa1_b", w) * CG[2]
-                qo = lin(ln(c) * CG[3] + CG[4], "qcr1_w", "qcr1_b", w)
+                fk.vec_gate_residual_(c, mod_lin(CG[0], CG[1], "msa1_w", "msa1_b", w), CG[2])
+                qo = mod_lin(CG[3], CG[4], "qcr1_w", "qcr1_b", w)                  # bf16 [2D]
                 q_cc, x_const = qo[:D], qo[D:]
                 kv_x = F.linear(h_mod, w["kvx_w"], w["kvx_b"])                     # [N, 2D]
-                o1 = fk.attention_1q(q_cc, kv_x, H, HD)                            # [D]
-                h_mod = fk.fast_gate_add_and_modulate(x, x_const.to(BF16), G[b, 5], G[b, 6], G[b, 7],
-                                                      broadcast_h=True)
-                c = c + lin(o1, "cond_to_out_cross", "cond_to_out_cross_b", w) * CG[5]
-                a_g = lin(ln(c) * CG[6] + CG[7], "cond_ffn0", "cond_ffn0_b", w)
-                a, g = a_g.chunk(2)
-                c = c + lin(F.silu(g) * a, "cond_ffn1", "cond_ffn1_b", w) * CG[8]
+                o1 = fk.attention_1q(q_cc, kv_x, H, HD)                            # bf16 [D]
+                h_mod = fk.fast_gate_add_and_modulate(x, x_const, G[b, 5], G[b, 6], G[b, 7], broadcast_h=True)
+                fk.vec_gate_residual_(c, F.linear(o1, w["cond_to_out_cross"], w["cond_to_out_cross_b"]), CG[5])
+                a_g = mod_lin(CG[6], CG[7], "cond_ffn0", "cond_ffn0_b", w)        # bf16 [2F]
+                y = fk.fast_swiglu_from_packed(a_g.view(1, -1))                     # silu(g) * a, bf16
+                fk.vec_gate_residual_(c, F.linear(y, w["cond_ffn1"], w["cond_ffn1_b"]), CG[8])
             else:
-                if ln_c is None:
-                    ln_c = ln(c)
+                # the context vector is frozen from here on; LN(c) is recomputed per block (one launch)
                 C2 = CG2[b - cd]
-                x_const = lin(ln_c * C2[0] + C2[1], "cr1_w", "cr1_b", w)
-                h_mod = fk.fast_gate_add_and_modulate(x, x_const.to(BF16), G[b, 5], G[b, 6], G[b, 7],
-                                                      broadcast_h=True)
+                x_const = mod_lin(C2[0], C2[1], "cr1_w", "cr1_b", w)
+                h_mod = fk.fast_gate_add_and_modulate(x, x_const, G[b, 5], G[b, 6], G[b, 7], broadcast_h=True)
             hf = self._ffn(b, h_mod, geom)
             if b + 1 < self.depth:
                 h_mod = fk.fast_gate_add_and_modulate(x, hf, G[b, 8], G[b + 1, 0], G[b + 1, 1])

@@ -209,6 +209,20 @@ def fused_qknorm_rope2d_cond_inplace(qkv: torch.Tensor, q_scale: torch.Tensor, k
     return qkv
 
 
+def vec_ln_modulate(v: torch.Tensor, scale1: torch.Tensor, shift: torch.Tensor) -> torch.Tensor:
+    """bf16 LN(v) * scale1 + shift of one fp32 [D] vector (the 1-token context stream)."""
+    v = v.reshape(-1)
+    out = torch.empty(v.numel(), dtype=BF16, device=v.device)
+    check(lib().vdit_vec_ln_modulate(ptr(v), v.numel(), ptr(scale1), ptr(shift), ptr(out), _s(v)), "vec_ln_modulate")
+    return out
+
+
+def vec_gate_residual_(c: torch.Tensor, y: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+    """c += float(y) * gate in place (fp32 [D] vector, bf16 update)."""
+    check(lib().vdit_vec_gate_residual(ptr(c), ptr(y.reshape(-1)), ptr(gate), c.numel(), _s(c)), "vec_gate_residual")
+    return c
+
+
 def fast_swiglu_from_packed(h_packed: torch.Tensor) -> torch.Tensor:
     """silu(h[:, F:]) * h[:, :F] (``lib/fast_kernels.py:942-974``)."""
     m, f2 = h_packed.shape

@@ -124,6 +124,14 @@ int vdit_qknorm_rope2d(void* qkv, int64_t l, int32_t heads, int32_t head_dim, co
                        const float* k_scale, const float* cos2d, const float* sin2d,
                        int32_t n_prefix, vdit_stream_t stream);
 
+/* Context-vector steps of the exact 1-token uncond branch (the reference runs them
+ * as torch element-wise ops on the [D] fp32 context vector, lib/fast_flow.py:1702-1794,
+ * 2295-2309).  vdit_vec_ln_modulate: out bf16 [d] = LN(v)*s1 + sh with eps 1e-6
+ * (v fp32 [d], d <= 2048).  vdit_vec_gate_residual: c[d] fp32 += float(y[d] bf16) * g[d]. */
+int vdit_vec_ln_modulate(const float* v, int32_t d, const float* s1, const float* sh, void* out,
+                         vdit_stream_t stream);
+int vdit_vec_gate_residual(float* c, const void* y, const float* g, int32_t d, vdit_stream_t stream);
+
 /* out[m,f] = silu(h[:, f:2f]) * h[:, :f] from packed h [m,2f] bf16.  Replaces
  * _fused_packed_swiglu_kernel (lib/fast_kernels.py:650-669, 942-974). */
 int vdit_swiglu_packed(const void* h, int64_t m, int32_t f, void* out, vdit_stream_t stream);
