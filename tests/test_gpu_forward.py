@@ -97,3 +97,33 @@ def test_graph_replay_matches_eager():
         assert rel(graphed, eager) < 1e-4
     assert len(runner._graphs) == 1
     assert _lib.device_error() == 0
+
+
+def test_one_nfe_large_n_matches_oracle():
+    """N = 32768 voxels of an ellipsoid-shell union in 128^3 (eight 4096-voxel windows,
+    the production window size, the staged conv over 256 blocks): one NFE of each branch."""
+    from vdit.workloads import ellipsoid_union
+    dim, hd = 256, 128
+    cfg = om.ModelConfig(dim=dim, head_dim=hd, depth=2, cond_depth=1, res=128, patch_size=4096)
+    p = om.init_params(cfg, 21, weight_std=0.03, bias_std=0.02, scale_jitter=0.1)
+    mc = {"dim": dim, "head_dim": hd, "depth": 2, "cond_depth": 1, "res": 128, "patch_size": 4096,
+          "latent_scale": cfg.latent_scale}
+    runner = OptimizedLatDitRunner(LatDitModel.from_state_dict(p, mc), SolverConfig(guidance_scale=3.0),
+                                   device=torch.device(DEV))
+    vox = ellipsoid_union(32768, 128, 3)
+    assert len(vox) == 32768
+    g = torch.Generator().manual_seed(22)
+    ctx = torch.randn(5 + 64, dim, generator=g)
+    xt = torch.randn(len(vox), 16, generator=g)
+    geom_o = om.build_geometry(vox, cfg)
+    xs = xt[geom_o.perm]
+    t = 0.9
+    pos_o = om.flow_forward(p, cfg, xs, t, ctx, geom_o)
+    neg_o = om.flow_forward_1tok(p, cfg, xs, t, geom_o)
+    ctx_d = ctx.to(DEV, torch.bfloat16)
+    geom = runner._prepare_sample_geometry([torch.from_numpy(vox).to(DEV)], ctx_d)
+    assert torch.equal(geom["perm"].cpu(), geom_o.perm)
+    xs_d = xs.to(DEV)
+    assert rel(runner.forward_flow_fast(xs_d, t, ctx_d, None, geom), pos_o) < 1e-2
+    assert rel(runner.forward_flow_fast(xs_d, t, ctx_d, None, geom, uncond=True), neg_o) < 1e-2
+    assert _lib.device_error() == 0
