@@ -92,6 +92,9 @@ class OptimizedLatDitRunner:
         # when a list, every window self-attention launch appends (start event, end event,
         # window sizes) to it -- the benchmark's in-step measurement of that kernel
         self.attention_timer: Optional[list] = None
+        # the context stream of the context blocks runs on its own CUDA stream
+        self.overlap_context = True
+        self._ctx_stream: Optional[torch.cuda.Stream] = None
         # CUDA-graph replay of the sampler (per voxel count, context length and schedule)
         self.cuda_graph = bool(cuda_graph)
         self._graphs: "OrderedDict[tuple, _SampleGraph]" = OrderedDict()
@@ -289,27 +292,53 @@ class OptimizedLatDitRunner:
         h_mod = fk.fast_modulate(x, None, G[0, 0], G[0, 1])
         c_mod = fk.fast_modulate(c, None, CG9[0, 0], CG9[0, 1]) if cd > 0 else None
         share = self.solver_config.ditfastattn_b0_msa_share
+        # The context stream of the context blocks runs on a second CUDA stream: it meets the
+        # voxel stream only at the cross-attention (q/k/v of both sides) and after the last
+        # context block (the frozen context feeds the remaining blocks).  Tensors that cross
+        # streams are recorded on the stream that reads them.
+        main = torch.cuda.current_stream(self.device)
+        side = self._context_stream() if (cd > 0 and self.overlap_context) else main
+        if side is not main:
+            side.wait_stream(main)
+            c.record_stream(side)
+            c_mod.record_stream(side)
         for b in range(self.depth):
             w = self.blocks[b]
+            if b < cd:
+                CG = CG9[b]
+                with torch.cuda.stream(side):
+                    qkvc = F.linear(c_mod, w["cond_to_qkv"], w["cond_to_qkv_b"])
+                    fk.fused_qknorm_rope2d_cond_inplace(qkvc, w["cqs"], w["cks"], cos2, sin2, H, HD, n_prefix=5)
+                    oc = fk.flash_cond_self_attn(qkvc, H, HD)
+                    hc = F.linear(oc, w["cond_to_out"], w["cond_to_out_b"])
+                    c_mod = fk.fast_gate_add_and_modulate(c, hc, CG[2], CG[3], CG[4])
+                    qkvcc = F.linear(c_mod, w["cond_to_qkv_cross"], w["cond_to_qkv_cross_b"])
             h = self._self_attention(b, h_mod, geom)
             h_mod = fk.fast_gate_add_and_modulate(x, h, G[b, 2], G[b, 3], G[b, 4])
             if b == 0 and share:
                 self._b0_share = (round(float(t_val), 7), x.clone())
             if b < cd:
-                CG = CG9[b]
-                qkvc = F.linear(c_mod, w["cond_to_qkv"], w["cond_to_qkv_b"])
-                fk.fused_qknorm_rope2d_cond_inplace(qkvc, w["cqs"], w["cks"], cos2, sin2, H, HD, n_prefix=5)
-                oc = fk.flash_cond_self_attn(qkvc, H, HD)
-                hc = F.linear(oc, w["cond_to_out"], w["cond_to_out_b"])
-                c_mod = fk.fast_gate_add_and_modulate(c, hc, CG[2], CG[3], CG[4])
                 qkvx = F.linear(h_mod, w["to_qkv_cross"], w["to_qkv_cross_b"])
-                qkvcc = F.linear(c_mod, w["cond_to_qkv_cross"], w["cond_to_qkv_cross_b"])
+                if side is not main:
+                    main.wait_stream(side)                 # qkvcc is ready
+                    qkvcc.record_stream(main)
+                    side.wait_stream(main)                 # qkvx is ready
+                    qkvx.record_stream(side)
+                with torch.cuda.stream(side):
+                    ocx = fk.attention(qkvcc[:, :D], qkvx[:, D:2 * D], qkvx[:, 2 * D:], [0, L], [0, N], H, HD)
+                    hcx = F.linear(ocx, w["cond_to_out_cross"], w["cond_to_out_cross_b"])
+                    c_mod = fk.fast_gate_add_and_modulate(c, hcx, CG[5], CG[6], CG[7])
+                    hc2 = F.linear(c_mod, w["cond_ffn0"], w["cond_ffn0_b"])
+                    hcf = F.linear(fk.fast_swiglu_from_packed(hc2), w["cond_ffn1"], w["cond_ffn1_b"])
+                    if b + 1 < cd:
+                        c_mod = fk.fast_gate_add_and_modulate(c, hcf, CG[8], CG9[b + 1, 0], CG9[b + 1, 1])
+                    else:
+                        fk.fast_gate_add(c, hcf, CG[8])
                 ox = fk.attention(qkvx[:, :D], qkvcc[:, D:2 * D], qkvcc[:, 2 * D:], [0, N], [0, L], H, HD)
-                ocx = fk.attention(qkvcc[:, :D], qkvx[:, D:2 * D], qkvx[:, 2 * D:], [0, L], [0, N], H, HD)
                 hx = F.linear(ox, w["to_out_cross"], w["to_out_cross_b"])
                 h_mod = fk.fast_gate_add_and_modulate(x, hx, G[b, 5], G[b, 6], G[b, 7])
-                hcx = F.linear(ocx, w["cond_to_out_cross"], w["cond_to_out_cross_b"])
-                c_mod = fk.fast_gate_add_and_modulate(c, hcx, CG[5], CG[6], CG[7])
+                if b + 1 == cd and side is not main:
+                    main.wait_stream(side)                 # the frozen context for the remaining blocks
             else:
                 C2 = CG2[b - cd]
                 q = F.linear(h_mod, w["to_q_cross"], w["to_q_cross_b"])
@@ -323,15 +352,14 @@ class OptimizedLatDitRunner:
                 h_mod = fk.fast_gate_add_and_modulate(x, hf, G[b, 8], G[b + 1, 0], G[b + 1, 1])
             else:
                 fk.fast_gate_add(x, hf, G[b, 8])
-            if b < cd:
-                CG = CG9[b]
-                hc2 = F.linear(c_mod, w["cond_ffn0"], w["cond_ffn0_b"])
-                hcf = F.linear(fk.fast_swiglu_from_packed(hc2), w["cond_ffn1"], w["cond_ffn1_b"])
-                if b + 1 < cd:
-                    c_mod = fk.fast_gate_add_and_modulate(c, hcf, CG[8], CG9[b + 1, 0], CG9[b + 1, 1])
-                else:
-                    fk.fast_gate_add(c, hcf, CG[8])
+        if side is not main:
+            main.wait_stream(side)
         return fk.fast_out_modulate_unpatchify(x, None, OG[0], OG[1], self.W_unpatch)
+
+    def _context_stream(self) -> torch.cuda.Stream:
+        if self._ctx_stream is None:
+            self._ctx_stream = torch.cuda.Stream(self.device)
+        return self._ctx_stream
 
     def _forward_uncond_1tok(self, xt_sorted: torch.Tensor, t_val: float, geom) -> torch.Tensor:
         """Exact zero-context branch with a 1-token context stream (fp32 vector)."""
