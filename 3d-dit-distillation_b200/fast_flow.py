@@ -334,16 +334,20 @@ class OptimizedLatDitRunner:
                         c_mod = fk.fast_gate_add_and_modulate(c, hcf, CG[8], CG9[b + 1, 0], CG9[b + 1, 1])
                     else:
                         fk.fast_gate_add(c, hcf, CG[8])
+                    if b + 1 == cd:
+                        # the context is frozen from here on: the K/V of every remaining block
+                        kv_frozen = self._frozen_context_kv(c, CG2)
                 ox = fk.attention(qkvx[:, :D], qkvcc[:, D:2 * D], qkvcc[:, 2 * D:], [0, N], [0, L], H, HD)
                 hx = F.linear(ox, w["to_out_cross"], w["to_out_cross_b"])
                 h_mod = fk.fast_gate_add_and_modulate(x, hx, G[b, 5], G[b, 6], G[b, 7])
-                if b + 1 == cd and side is not main:
-                    main.wait_stream(side)                 # the frozen context for the remaining blocks
             else:
-                C2 = CG2[b - cd]
+                if cd == 0 and b == 0:
+                    kv_frozen = self._frozen_context_kv(c, CG2)
                 q = F.linear(h_mod, w["to_q_cross"], w["to_q_cross_b"])
-                cm = fk.fast_modulate(c, None, C2[0], C2[1])
-                kv = F.linear(cm, w["cond_to_kv_cross"], w["cond_to_kv_cross_b"])
+                kv, ready = kv_frozen[b - cd]
+                if side is not main:
+                    main.wait_event(ready)
+                    kv.record_stream(main)
                 ox = fk.attention(q, kv[:, :D], kv[:, D:], [0, N], [0, L], H, HD)
                 hx = F.linear(ox, w["to_out_cross"], w["to_out_cross_b"])
                 h_mod = fk.fast_gate_add_and_modulate(x, hx, G[b, 5], G[b, 6], G[b, 7])
@@ -355,6 +359,20 @@ class OptimizedLatDitRunner:
         if side is not main:
             main.wait_stream(side)
         return fk.fast_out_modulate_unpatchify(x, None, OG[0], OG[1], self.W_unpatch)
+
+    def _frozen_context_kv(self, c: torch.Tensor, CG2) -> list:
+        """K/V of the frozen context for every block after the context blocks, queued on the
+        current stream (the context stream); each comes with an event the voxel stream waits on."""
+        out = []
+        for b in range(self.cond_depth, self.depth):
+            C2 = CG2[b - self.cond_depth]
+            w = self.blocks[b]
+            cm = fk.fast_modulate(c, None, C2[0], C2[1])
+            kv = F.linear(cm, w["cond_to_kv_cross"], w["cond_to_kv_cross_b"])
+            ev = torch.cuda.Event()
+            ev.record()
+            out.append((kv, ev))
+        return out
 
     def _context_stream(self) -> torch.cuda.Stream:
         if self._ctx_stream is None:
@@ -371,6 +389,7 @@ class OptimizedLatDitRunner:
                                    and self._b0_share[0] == key
                                    and self._b0_share[1].shape[0] == xt_sorted.shape[0]) else None
         c = torch.zeros(D, dtype=F32, device=xt_sorted.device)
+        main = side = torch.cuda.current_stream(self.device)
 
         def mod_lin(scale1, shift, wk, bk, blk):
             """bf16 Linear(LN(c) * scale1 + shift) of the context vector."""
@@ -402,15 +421,34 @@ class OptimizedLatDitRunner:
                 y = fk.fast_swiglu_from_packed(a_g.view(1, -1))                     # silu(g) * a, bf16
                 fk.vec_gate_residual_(c, F.linear(y, w["cond_ffn1"], w["cond_ffn1_b"]), CG[8])
             else:
-                # the context vector is frozen from here on; LN(c) is recomputed per block (one launch)
-                C2 = CG2[b - cd]
-                x_const = mod_lin(C2[0], C2[1], "cr1_w", "cr1_b", w)
+                if b == cd:
+                    # the context vector is frozen from here on: the constant cross-attention
+                    # output of every remaining block, on the context stream, one event each
+                    main = torch.cuda.current_stream(self.device)
+                    side = self._context_stream() if self.overlap_context else main
+                    if side is not main:
+                        side.wait_stream(main)
+                        c.record_stream(side)
+                    with torch.cuda.stream(side):
+                        consts = []
+                        for bb in range(cd, self.depth):
+                            C2 = CG2[bb - cd]
+                            xc = mod_lin(C2[0], C2[1], "cr1_w", "cr1_b", self.blocks[bb])
+                            ev = torch.cuda.Event()
+                            ev.record()
+                            consts.append((xc, ev))
+                x_const, ready = consts[b - cd]
+                if side is not main:
+                    main.wait_event(ready)
+                    x_const.record_stream(main)
                 h_mod = fk.fast_gate_add_and_modulate(x, x_const, G[b, 5], G[b, 6], G[b, 7], broadcast_h=True)
             hf = self._ffn(b, h_mod, geom)
             if b + 1 < self.depth:
                 h_mod = fk.fast_gate_add_and_modulate(x, hf, G[b, 8], G[b + 1, 0], G[b + 1, 1])
             else:
                 fk.fast_gate_add(x, hf, G[b, 8])
+        if self.depth > cd and side is not main:
+            main.wait_stream(side)
         return fk.fast_out_modulate_unpatchify(x, None, OG[0], OG[1], self.W_unpatch)
 
     # ------------------------------------------------------------------ sampler
