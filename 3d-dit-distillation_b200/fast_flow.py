@@ -389,11 +389,25 @@ class OptimizedLatDitRunner:
                                    and self._b0_share[0] == key
                                    and self._b0_share[1].shape[0] == xt_sorted.shape[0]) else None
         c = torch.zeros(D, dtype=F32, device=xt_sorted.device)
-        main = side = torch.cuda.current_stream(self.device)
+        # The context vector's chain (modulated GEMVs, the single query over the voxels, the
+        # context FFN) runs on the context stream; it meets the voxel stream at the constant
+        # cross-attention output (needed by the voxel gate-add) and at the voxel K/V (read by
+        # the single-query attention).  Tensors that cross streams are recorded on the reader.
+        main = torch.cuda.current_stream(self.device)
+        side = self._context_stream() if self.overlap_context else main
+        two = side is not main
+        if two:
+            side.wait_stream(main)
+            c.record_stream(side)
 
         def mod_lin(scale1, shift, wk, bk, blk):
             """bf16 Linear(LN(c) * scale1 + shift) of the context vector."""
             return F.linear(fk.vec_ln_modulate(c, scale1, shift), blk[wk], blk[bk])
+
+        def on_side_event():
+            ev = torch.cuda.Event()
+            ev.record()
+            return ev
 
         if share is not None:
             x = share[1].clone()
@@ -403,42 +417,47 @@ class OptimizedLatDitRunner:
             x = fk.patchify(xt_sorted, self.W_patch)
             h_mod = fk.fast_modulate(x, None, G[0, 0], G[0, 1])
             start = 0
+        consts = []
         for b in range(self.depth):
             w = self.blocks[b]
+            if b < cd:
+                CG = CG9[b]
+                with torch.cuda.stream(side):
+                    fk.vec_gate_residual_(c, mod_lin(CG[0], CG[1], "msa1_w", "msa1_b", w), CG[2])
+                    qo = mod_lin(CG[3], CG[4], "qcr1_w", "qcr1_b", w)              # bf16 [2D]
+                    q_cc, x_const = qo[:D], qo[D:]
+                    q_ready = on_side_event()
+            elif b == cd:
+                # the context vector is frozen from here on: the constant cross-attention output
+                # of every remaining block, one event each
+                with torch.cuda.stream(side):
+                    for bb in range(cd, self.depth):
+                        C2 = CG2[bb - cd]
+                        xc = mod_lin(C2[0], C2[1], "cr1_w", "cr1_b", self.blocks[bb])
+                        consts.append((xc, on_side_event()))
             if b >= start:
                 h = self._self_attention(b, h_mod, geom)
                 h_mod = fk.fast_gate_add_and_modulate(x, h, G[b, 2], G[b, 3], G[b, 4])
             if b < cd:
-                CG = CG9[b]
-                fk.vec_gate_residual_(c, mod_lin(CG[0], CG[1], "msa1_w", "msa1_b", w), CG[2])
-                qo = mod_lin(CG[3], CG[4], "qcr1_w", "qcr1_b", w)                  # bf16 [2D]
-                q_cc, x_const = qo[:D], qo[D:]
                 kv_x = F.linear(h_mod, w["kvx_w"], w["kvx_b"])                     # [N, 2D]
-                o1 = fk.attention_1q(q_cc, kv_x, H, HD)                            # bf16 [D]
+                if two:
+                    kv_ready = torch.cuda.Event()
+                    kv_ready.record(main)
+                    main.wait_event(q_ready)
+                    qo.record_stream(main)
                 h_mod = fk.fast_gate_add_and_modulate(x, x_const, G[b, 5], G[b, 6], G[b, 7], broadcast_h=True)
-                fk.vec_gate_residual_(c, F.linear(o1, w["cond_to_out_cross"], w["cond_to_out_cross_b"]), CG[5])
-                a_g = mod_lin(CG[6], CG[7], "cond_ffn0", "cond_ffn0_b", w)        # bf16 [2F]
-                y = fk.fast_swiglu_from_packed(a_g.view(1, -1))                     # silu(g) * a, bf16
-                fk.vec_gate_residual_(c, F.linear(y, w["cond_ffn1"], w["cond_ffn1_b"]), CG[8])
+                with torch.cuda.stream(side):
+                    if two:
+                        side.wait_event(kv_ready)
+                        kv_x.record_stream(side)
+                    o1 = fk.attention_1q(q_cc, kv_x, H, HD)                        # bf16 [D]
+                    fk.vec_gate_residual_(c, F.linear(o1, w["cond_to_out_cross"], w["cond_to_out_cross_b"]), CG[5])
+                    a_g = mod_lin(CG[6], CG[7], "cond_ffn0", "cond_ffn0_b", w)    # bf16 [2F]
+                    y = fk.fast_swiglu_from_packed(a_g.view(1, -1))                 # silu(g) * a, bf16
+                    fk.vec_gate_residual_(c, F.linear(y, w["cond_ffn1"], w["cond_ffn1_b"]), CG[8])
             else:
-                if b == cd:
-                    # the context vector is frozen from here on: the constant cross-attention
-                    # output of every remaining block, on the context stream, one event each
-                    main = torch.cuda.current_stream(self.device)
-                    side = self._context_stream() if self.overlap_context else main
-                    if side is not main:
-                        side.wait_stream(main)
-                        c.record_stream(side)
-                    with torch.cuda.stream(side):
-                        consts = []
-                        for bb in range(cd, self.depth):
-                            C2 = CG2[bb - cd]
-                            xc = mod_lin(C2[0], C2[1], "cr1_w", "cr1_b", self.blocks[bb])
-                            ev = torch.cuda.Event()
-                            ev.record()
-                            consts.append((xc, ev))
                 x_const, ready = consts[b - cd]
-                if side is not main:
+                if two:
                     main.wait_event(ready)
                     x_const.record_stream(main)
                 h_mod = fk.fast_gate_add_and_modulate(x, x_const, G[b, 5], G[b, 6], G[b, 7], broadcast_h=True)
@@ -447,7 +466,7 @@ class OptimizedLatDitRunner:
                 h_mod = fk.fast_gate_add_and_modulate(x, hf, G[b, 8], G[b + 1, 0], G[b + 1, 1])
             else:
                 fk.fast_gate_add(x, hf, G[b, 8])
-        if self.depth > cd and side is not main:
+        if two:
             main.wait_stream(side)
         return fk.fast_out_modulate_unpatchify(x, None, OG[0], OG[1], self.W_unpatch)
 
