@@ -90,11 +90,16 @@ class OptimizedLatDitRunner:
         self._rope_2d_cache: Dict[int, tuple] = {}
         self._b0_share = None
         # when a list, every window self-attention launch appends (start event, end event,
-        # window sizes) to it -- the benchmark's in-step measurement of that kernel
+        # window sizes, whether another NFE shared the GPU) to it -- the benchmark's in-step
+        # measurement of that kernel
         self.attention_timer: Optional[list] = None
+        self._nfe_shared = False
         # the context stream of the context blocks runs on its own CUDA stream
         self.overlap_context = True
-        self._ctx_stream: Optional[torch.cuda.Stream] = None
+        self._ctx_streams: Dict[int, torch.cuda.Stream] = {}
+        # the 1-token NFE of a guided step runs on its own stream beside the conditional one
+        self.overlap_branches = True
+        self._neg_stream: Optional[torch.cuda.Stream] = None
         # CUDA-graph replay of the sampler (per voxel count, context length and schedule)
         self.cuda_graph = bool(cuda_graph)
         self._graphs: "OrderedDict[tuple, _SampleGraph]" = OrderedDict()
@@ -260,7 +265,8 @@ class OptimizedLatDitRunner:
         if timer is not None:
             e1 = torch.cuda.Event(enable_timing=True)
             e1.record()
-            timer.append((e0, e1, [cu.host[i + 1] - cu.host[i] for i in range(len(cu.host) - 1)]))
+            timer.append((e0, e1, [cu.host[i + 1] - cu.host[i] for i in range(len(cu.host) - 1)],
+                          self._nfe_shared))
         return F.linear(o, w["to_out"], w["to_out_b"])
 
     def _ffn(self, b: int, h_mod: torch.Tensor, geom) -> torch.Tensor:
@@ -316,7 +322,10 @@ class OptimizedLatDitRunner:
             h = self._self_attention(b, h_mod, geom)
             h_mod = fk.fast_gate_add_and_modulate(x, h, G[b, 2], G[b, 3], G[b, 4])
             if b == 0 and share:
-                self._b0_share = (round(float(t_val), 7), x.clone())
+                x0 = x.clone()
+                ev0 = torch.cuda.Event()
+                ev0.record()
+                self._b0_share = (round(float(t_val), 7), x0, ev0)
             if b < cd:
                 qkvx = F.linear(h_mod, w["to_qkv_cross"], w["to_qkv_cross_b"])
                 if side is not main:
@@ -375,9 +384,12 @@ class OptimizedLatDitRunner:
         return out
 
     def _context_stream(self) -> torch.cuda.Stream:
-        if self._ctx_stream is None:
-            self._ctx_stream = torch.cuda.Stream(self.device)
-        return self._ctx_stream
+        """The context stream paired with the current stream (each NFE stream has its own)."""
+        key = torch.cuda.current_stream(self.device).cuda_stream
+        st = self._ctx_streams.get(key)
+        if st is None:
+            st = self._ctx_streams[key] = torch.cuda.Stream(self.device)
+        return st
 
     def _forward_uncond_1tok(self, xt_sorted: torch.Tensor, t_val: float, geom) -> torch.Tensor:
         """Exact zero-context branch with a 1-token context stream (fp32 vector)."""
@@ -410,6 +422,9 @@ class OptimizedLatDitRunner:
             return ev
 
         if share is not None:
+            cur = torch.cuda.current_stream(self.device)
+            cur.wait_event(share[2])                  # block 0 of the conditional NFE is done
+            share[1].record_stream(cur)
             x = share[1].clone()
             h_mod = fk.fast_modulate(x, None, G[0, 3], G[0, 4])
             start = 1
@@ -532,14 +547,31 @@ class OptimizedLatDitRunner:
                       guided: List[bool], g_scale: float) -> torch.Tensor:
         """GPU part of the sampler: Euler + CFG over the schedule, latents in input order."""
         xt = fk.gather_rows_f32(noise, geom["perm"])
+        main = torch.cuda.current_stream(self.device)
         for i in range(len(guided)):
+            both = guided[i] and g_scale > 0
+            neg = self._negative_stream() if (both and self.overlap_branches) else main
+            if neg is not main:
+                neg.wait_stream(main)                     # x_t of this step
+                xt.record_stream(neg)
+            self._nfe_shared = neg is not main
             v = self.forward_flow_fast(xt, tl[i], context, None, geom)
             vn = None
-            if guided[i] and g_scale > 0:
-                vn = self.forward_flow_fast(xt, tl[i], context, None, geom, uncond=True)
+            if both:
+                with torch.cuda.stream(neg):
+                    vn = self.forward_flow_fast(xt, tl[i], context, None, geom, uncond=True)
+                if neg is not main:
+                    main.wait_stream(neg)
+                    vn.record_stream(main)
             fk.cfg_euler_(xt, v, vn, g_scale, tl[i] - tl[i + 1])
+        self._nfe_shared = False
         self._b0_share = None
         return fk.unpermute_denorm(xt, geom["up_widx"], self._denorm_scale, self._denorm_shift)
+
+    def _negative_stream(self) -> torch.cuda.Stream:
+        if self._neg_stream is None:
+            self._neg_stream = torch.cuda.Stream(self.device)
+        return self._neg_stream
 
     def _capture_sample(self, key, geom, context, noise, tl, guided, g_scale) -> "_SampleGraph":
         """Run the sample once eagerly on a side stream (first-call set-up of every kernel,

@@ -495,9 +495,13 @@ def main():
     tflops_sustained = _peaks_sustained()
     # live: average duration of the window self-attention launches inside the timed steps
     # (CUDA events on their stream), against the sustained GEMM peak
-    live_ms = statistics.fmean(a.elapsed_time(b) for a, b, _ in att_events)
-    flops = statistics.fmean(sum(4.0 * n * n * w.arch.dim for n in sizes) for _, _, sizes in att_events)
+    live_ms = statistics.fmean(a.elapsed_time(b) for a, b, _, _ in att_events)
+    flops = statistics.fmean(sum(4.0 * n * n * w.arch.dim for n in sizes) for _, _, sizes, _ in att_events)
     achieved = flops / (live_ms / 1e3) / 1e12
+    # the same launches restricted to steps where only one NFE runs (the unguided step):
+    # in guided steps the conditional and the 1-token NFE run on two streams and share the GPU
+    solo = [(a, b, sz) for a, b, sz, shared in att_events if not shared]
+    solo_ms = statistics.fmean(a.elapsed_time(b) for a, b, _ in solo) if solo else None
     flops_alone, att_ms_alone = attention_roofline(w, runner)
     traffic = None
     tp = ROOT / "profiles" / "fmha_traffic.json"
@@ -534,6 +538,11 @@ def main():
                          "peak_kind": f"{peak_kind} sustained bf16 (kernel timed inside the timed steps)",
                          "flops_per_launch": flops, "ms_per_launch": live_ms, "launches": len(att_events),
                          "traffic": traffic,
+                         "unshared": None if solo_ms is None else {
+                             "ms_per_launch": solo_ms, "launches": len(solo),
+                             "achieved": flops / (solo_ms / 1e3) / 1e12,
+                             "frac": flops / (solo_ms / 1e3) / 1e12 / tflops_sustained,
+                             "note": "launches of the unguided step, where no second NFE shares the GPU"},
                          "alone": {"ms_per_launch": att_ms_alone,
                                    "achieved": flops_alone / (att_ms_alone / 1e3) / 1e12,
                                    "peak": tflops_peak, "peak_kind": f"{peak_kind} burst bf16",
