@@ -136,10 +136,12 @@ def cpu_baseline_sample(threads: int):
 
 
 def run_reference(args):
-    """--impl reference: the reference algorithm on the host CPU (oracle port)."""
+    """--impl reference: the reference algorithm on the host CPU (oracle port).  Only the
+    workload generator of the package is used (the same voxel sets as the GPU arm)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    load_package()
     threads = os.cpu_count() or 1
     for _ in range(args.warmup):
         cpu_baseline_sample(threads)
