@@ -37,6 +37,8 @@ def _f32(v: torch.Tensor) -> torch.Tensor:
 
 def lex_perm(vox: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """(perm, up_widx, h_coords) of one sample, ``lib/fast_flow.py:667-694``."""
+    if vox.dim() != 2 or vox.shape[1] != 3:
+        raise ValueError(f"voxel coordinates must be [N, 3] (x, y, z), got {tuple(vox.shape)}")
     vox = vox.to(torch.int32).contiguous()
     n = vox.shape[0]
     dev = vox.device

@@ -62,6 +62,13 @@ def test_shape_errors_are_reported_before_any_launch():
         _lib.check(-1, "probe")
 
 
+def test_voxel_coordinates_must_be_n_by_3():
+    from vdit import fast_kernels as fk
+    for bad in (torch.zeros(10, 4, dtype=torch.int32), torch.zeros(10, dtype=torch.int32)):
+        with pytest.raises(ValueError, match=r"\[N, 3\]"):
+            fk.lex_perm(bad)
+
+
 @pytest.mark.parametrize("steps,guided", [(4, 3), (8, 6), (14, None)])
 def test_build_schedule_matches_oracle(steps, guided):
     cfg = SolverConfig(num_inference_steps=steps, n_guided_steps=guided or 10,
