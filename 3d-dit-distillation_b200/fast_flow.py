@@ -240,6 +240,8 @@ class OptimizedLatDitRunner:
         conv_plan = fk.build_conv_plan(conv_indices, order_caches[0][0]) if self.ffn_interleaved else None
         L = context.shape[-2]
         cond_size = int(round(math.sqrt(max(L - 5, 0))))
+        if L > 5 and cond_size * cond_size != L - 5:
+            raise ValueError(f"context of {L} tokens: expected 5 prefix tokens and a square grid of image tokens")
         cos2, sin2 = self._get_rope_2d_table(cond_size) if L > 5 else (None, None)
         return {"N": N, "batch_size": 1, "sizes": [N], "layout": [slice(0, N)], "perm": perm, "up_widx": up_widx,
                 "h_coords": h_coords, "cos_vox": self.cos3, "sin_vox": self.sin3, "cos_cond_2d": cos2,

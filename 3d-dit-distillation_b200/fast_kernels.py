@@ -206,6 +206,9 @@ def fused_qknorm_rope2d_cond_inplace(qkv: torch.Tensor, q_scale: torch.Tensor, k
     """Context tokens in place: RMS(q,k)*scale, 2D RoPE on tokens >= 5
     (``lib/fast_kernels.py:1412-1473``)."""
     l = qkv.shape[0]
+    need = max(l - n_prefix, 0) * 2 * (head_dim // 4)      # (token, axis) rows x hd/4 frequencies
+    if need and (cos2d is None or sin2d is None or cos2d.numel() < need or sin2d.numel() < need):
+        raise ValueError(f"2D RoPE tables cover fewer than the {l - n_prefix} rotated context tokens")
     check(lib().vdit_qknorm_rope2d(ptr(qkv), l, heads, head_dim, ptr(q_scale), ptr(k_scale), ptr(cos2d), ptr(sin2d),
                                    n_prefix, _s(qkv)), "qknorm_rope2d")
     return qkv

@@ -62,6 +62,13 @@ def test_shape_errors_are_reported_before_any_launch():
         _lib.check(-1, "probe")
 
 
+def test_rope2d_tables_must_cover_the_context():
+    qkv = torch.zeros(5 + 10, 3 * 256, dtype=torch.bfloat16)
+    cos, sin = torch.zeros(9, 2, 32), torch.zeros(9, 2, 32)         # a 3x3 grid: 9 of the 10 tokens
+    with pytest.raises(ValueError, match="RoPE tables"):
+        fk.fused_qknorm_rope2d_cond_inplace(qkv, torch.ones(256), torch.ones(256), cos, sin, 2, 128)
+
+
 def test_voxel_coordinates_must_be_n_by_3():
     from vdit import fast_kernels as fk
     for bad in (torch.zeros(10, 4, dtype=torch.int32), torch.zeros(10, dtype=torch.int32)):
