@@ -296,6 +296,21 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_q: Sequence[
     ``out_rows`` scatters output row i to out_rows[i]."""
     if out is None:
         out = torch.empty(q.shape[0], heads * head_dim, dtype=BF16, device=q.device)
+    for t, name in ((q, "q"), (k, "k"), (v, "v"), (out, "out")):
+        if t.dtype != BF16 or t.dim() != 2:
+            raise ValueError(f"attention: {name} must be a 2D bf16 view, got {tuple(t.shape)} {t.dtype}")
+    if len(cu_q) != len(cu_k) or len(cu_q) < 2:
+        raise ValueError("attention: cu_q and cu_k need the same number (>= 2) of offsets")
+    # the kernel reads rows [0, cu[-1]) through tensor maps built from these offsets
+    if int(cu_q[-1]) > q.shape[0] or int(cu_k[-1]) > k.shape[0] or int(cu_k[-1]) > v.shape[0]:
+        raise ValueError(f"attention: offsets end at {int(cu_q[-1])}/{int(cu_k[-1])} rows, past q/k/v "
+                         f"of {q.shape[0]}/{k.shape[0]}/{v.shape[0]} rows")
+    if out_rows is None and int(cu_q[-1]) > out.shape[0]:
+        raise ValueError(f"attention: out has {out.shape[0]} rows, fewer than the {int(cu_q[-1])} query rows")
+    if out_rows is not None and out_rows.dtype != torch.int64:
+        raise ValueError(f"attention: out_rows must be int64, got {out_rows.dtype}")
+    if out_rows is not None and out_rows.numel() < int(cu_q[-1]):
+        raise ValueError(f"attention: out_rows has {out_rows.numel()} entries for {int(cu_q[-1])} query rows")
     nseg = len(cu_q) - 1
     cq, ck = _host_i32(cu_q), _host_i32(cu_k)      # host arrays, alive for the call
     scale = 1.0 / math.sqrt(head_dim) if scale is None else scale
@@ -347,6 +362,10 @@ def attention_1q(q: torch.Tensor, kv: torch.Tensor, heads: int, head_dim: int,
     (``lib/fast_flow.py:1769-1777``)."""
     d = heads * head_dim
     v_offset = k_offset + d if v_offset is None else v_offset
+    if kv.dtype != BF16 or kv.dim() != 2 or q.numel() != d:
+        raise ValueError(f"attention_1q: kv must be 2D bf16 and q hold {d} values")
+    if min(k_offset, v_offset) < 0 or max(k_offset, v_offset) + d > kv.shape[1]:
+        raise ValueError(f"attention_1q: K/V columns at {k_offset}/{v_offset} run past the {kv.shape[1]} of kv")
     n = kv.shape[0]
     ws = torch.empty(int(lib().vdit_attention_1q_workspace_bytes(heads, head_dim, n)), dtype=torch.uint8,
                      device=kv.device)

@@ -69,6 +69,20 @@ def test_rope2d_tables_must_cover_the_context():
         fk.fused_qknorm_rope2d_cond_inplace(qkv, torch.ones(256), torch.ones(256), cos, sin, 2, 128)
 
 
+def test_attention_offsets_must_stay_inside_the_tensors():
+    q = torch.zeros(100, 256, dtype=torch.bfloat16)
+    kv = torch.zeros(60, 512, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="past q/k/v"):
+        fk.attention(q, kv[:, :256], kv[:, 256:], [0, 50, 100], [0, 30, 61], 2, 128)
+    with pytest.raises(ValueError, match="out_rows"):
+        fk.attention(q, kv[:, :256], kv[:, 256:], [0, 100], [0, 60], 2, 128,
+                     out_rows=torch.arange(99))
+    with pytest.raises(ValueError, match="same number"):
+        fk.attention(q, kv[:, :256], kv[:, 256:], [0, 100], [0, 30, 60], 2, 128)
+    with pytest.raises(ValueError, match="run past"):
+        fk.attention_1q(torch.zeros(256, dtype=torch.bfloat16), kv, 2, 128, k_offset=256)
+
+
 def test_voxel_coordinates_must_be_n_by_3():
     from vdit import fast_kernels as fk
     for bad in (torch.zeros(10, 4, dtype=torch.int32), torch.zeros(10, dtype=torch.int32)):
