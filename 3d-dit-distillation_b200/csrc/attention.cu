@@ -454,6 +454,7 @@ namespace vdit {
 int dense_conv_error_word(int clear);   // error word of the dense conv kernel (dense_conv.cu)
 int dwconv_plan_error_word(int clear);  // error word of the staged depthwise conv (dwconv_plan.cu)
 int rowops_error_word(int clear);       // error word of the staged row kernels (rowops.cu)
+int gemm_error_word(int clear);         // error word of the tcgen05 GEMM (gemm.cu)
 }
 
 extern "C" int vdit_device_error(int clear) {
@@ -470,5 +471,7 @@ extern "C" int vdit_device_error(int clear) {
     if (p < 0) return p;
     const int r = vdit::rowops_error_word(clear);
     if (r < 0) return r;
-    return v != 0 ? v : (d != 0 ? d : (p != 0 ? p : r));
+    const int g = vdit::gemm_error_word(clear);
+    if (g < 0) return g;
+    return v != 0 ? v : (d != 0 ? d : (p != 0 ? p : (r != 0 ? r : g)));
 }

@@ -1,0 +1,337 @@
+// Persistent bf16 GEMM on tcgen05 tensor cores for the block linears:
+//   C[M, N] = A[M, K] . W[N, K]^T + bias[N]        (nn.Linear / F.linear layout)
+// with epilogues fused where the result feeds a row operation.
+//
+// CTA pairs (clusters of two, cta_group::2): a pair computes a 256 x 256 output tile
+// with 256 x 256 x 16 MMAs issued by the even CTA; each CTA stages its own 128 rows
+// of A and its own 128 rows (output columns) of W, so each SM's shared memory feeds
+// half the weight tile the pair multiplies.  Pairs walk the tiles t, t + pairs, ...
+// (n-major, so the pairs working at one time share weight columns in L2).  Warp roles
+// in each CTA:
+//   warp 0      TMA producer: A box 64 x 128 and W box 64 x 128 (128-byte swizzle,
+//               K-major) per k-step into a 6-stage ring; both CTAs' loads complete on
+//               the even CTA's stage barrier, which expects the pair's bytes
+//   warp 1      MMA issuer (even CTA, one thread): four MMAs per k-step into one of two
+//               TMEM accumulators (2 x 256 fp32 columns = all 512, in both CTAs); its
+//               commits arrive on the stage / accumulator barriers of both CTAs
+//   warps 2..5  epilogue: warp w drains TMEM lane quarter w % 4 (32 of the CTA's 128
+//               rows) while the MMAs of the next tile run into the other accumulator,
+//               then arrives on the even CTA's accumulator-free barrier
+// Every mbarrier wait is bounded; a wait that runs out records an error in
+// g_gemm_error, raises the CTA abort flag and the CTA skips to its teardown (cluster
+// barrier, TMEM always freed).
+#include <string.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace vdit {
+
+__device__ int g_gemm_error = 0;
+
+namespace gemm {
+
+using namespace tc;
+
+constexpr int BM = 128;             // rows per CTA (256 per pair)
+constexpr int BN = 256;             // output columns per pair tile
+constexpr int BNH = BN / 2;         // weight rows staged per CTA
+constexpr int BK = 64, STAGES = 6;
+constexpr int EPI_WARPS = 4;
+constexpr int THREADS = (2 + EPI_WARPS) * 32;
+constexpr uint32_t kStageBytes = (BM + BNH) * 128;   // per CTA and k-step
+constexpr int kErr = 0x474D;   // "GM": a bounded wait of the GEMM kernel ran out
+
+struct __align__(1024) Smem {
+    uint8_t a[STAGES][BM * 128];
+    uint8_t b[STAGES][BNH * 128];
+    uint8_t ostage[EPI_WARPS][2][32 * 128];   // per epilogue warp: two 32-row x 64-column bf16 boxes
+    uint64_t full[STAGES], empty[STAGES], acc_full[2], acc_empty[2];
+    uint32_t tmem_slot;
+    int abort_flag;
+};
+
+// epilogue kinds
+constexpr int EPI_BIAS = 0;   // out = bf16(acc + bias)
+
+struct EpiArgs {
+    const __nv_bfloat16* bias;   // [N] or null
+    __nv_bfloat16* out;
+    int64_t ldo;
+};
+
+// Banded tile order: the pairs walk GM m-tiles x all n-tiles before the next band,
+// so the A rows in flight (GM x 256 rows) stay in L2 while every weight column
+// passes over them (A of the ffn1 shape, 16384 x 3840, is larger than L2).
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
+    constexpr int GM = 8;
+    const int g = t / (GM * tiles_n), within = t - g * GM * tiles_n;
+    const int gm = min(GM, tiles_m - g * GM);
+    tm = g * GM + within % gm;
+    tn = within / gm;
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(x), "r"(y)
+                 : "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                          const __grid_constant__ CUtensorMap tmW,
+                                                          const __grid_constant__ CUtensorMap tmO, int64_t m, int n,
+                                                          int k, const __grid_constant__ EpiArgs ep) {
+    extern __shared__ uint8_t raw[];
+    Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    volatile int* abort_flag = &sm.abort_flag;
+    const int tiles_m = (int)((m + 2 * BM - 1) / (2 * BM)), tiles_n = n / BN;
+    const int ntiles = tiles_m * tiles_n;
+    const int nk = k / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&sm.full[s]), 1);
+            mbar_init(smem_u32(&sm.empty[s]), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&sm.acc_full[b]), 1);
+            mbar_init(smem_u32(&sm.acc_empty[b]), 2 * EPI_WARPS);
+        }
+        sm.abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmO)) : "memory");
+    }
+    if (warp == 1) {   // both CTAs of the pair allocate together (same warp, same slot offset)
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&sm.tmem_slot)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+        tc_fence_before();
+    }
+    __syncthreads();
+    cluster_sync();    // the peer's barriers are initialised before anyone signals them
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer (both CTAs)
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int t = pair; ok && t < ntiles; t += npairs) {
+                int tm, tn;
+                tile_coords(t, tiles_m, tiles_n, tm, tn);
+                const int arow = tm * 2 * BM + (int)rank * BM, wrow = tn * BN + (int)rank * BNH;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (it >= STAGES &&
+                        !mbar_wait(smem_u32(&sm.empty[s]), ((it / STAGES) - 1) & 1, abort_flag, &g_gemm_error, kErr)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t full_local = smem_u32(&sm.full[s]);
+                    if (leader) mbar_expect_tx(full_local, 2 * kStageBytes);
+                    const uint32_t bar = mapa_shared(full_local, 0);
+                    tma_load_2d_pair(smem_u32(sm.a[s]), &tmA, kb * BK, arow, bar);
+                    tma_load_2d_pair(smem_u32(sm.b[s]), &tmW, kb * BK, wrow, bar);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer (even CTA)
+        if (leader && lane == 0) {
+            constexpr uint32_t IDESC = make_idesc(2 * BM, BN, false);
+            int it = 0, lt = 0;
+            bool ok = true;
+            for (int t = pair; ok && t < ntiles; t += npairs, ++lt) {
+                const int buf = lt & 1;
+                if (lt >= 2 && !mbar_wait(smem_u32(&sm.acc_empty[buf]), ((lt >> 1) - 1) & 1, abort_flag,
+                                          &g_gemm_error, kErr))
+                    break;
+                tc_fence_after();
+                const uint32_t acc = tmem + buf * BN;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(smem_u32(&sm.full[s]), (it / STAGES) & 1, abort_flag, &g_gemm_error, kErr)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t abase = smem_u32(sm.a[s]), bbase = smem_u32(sm.b[s]);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        tc_mma_pair(acc, make_desc(abase + kk * 32, 16, 1024, kSw128),
+                                    make_desc(bbase + kk * 32, 16, 1024, kSw128), IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+                    tc_commit_pair(smem_u32(&sm.empty[s]), 0x3);
+                }
+                if (ok) tc_commit_pair(smem_u32(&sm.acc_full[buf]), 0x3);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        // Each warp turns 64 columns of its 32 rows at a time into bf16, writes them to one
+        // of its two staging boxes (128-byte swizzle: 16-byte chunk j of row r at chunk
+        // j ^ (r & 7), so the 32 lanes' stores spread over all banks) and one lane stores
+        // the box with TMA; rows past m are clipped by the tensor map.
+        const int ew = warp - 2;
+        const int quarter = warp & 3;
+        const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+        int lt = 0, nstore = 0;
+        for (int t = pair; t < ntiles; t += npairs, ++lt) {
+            const int buf = lt & 1;
+            int tm, tn;
+            tile_coords(t, tiles_m, tiles_n, tm, tn);
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sm.acc_full[buf]), (lt >> 1) & 1, abort_flag,
+                                                              &g_gemm_error, kErr));
+            if (!ok) break;
+            tc_fence_after();
+            const int row0 = tm * 2 * BM + (int)rank * BM + quarter * 32;
+            const int col0 = tn * BN;
+            if (EPI == EPI_BIAS) {
+#pragma unroll 1
+                for (int c = 0; c < BN / 64; ++c, ++nstore) {
+                    float v[64];
+                    tmem_ld32(tmem + buf * BN + c * 64 + lane_off, v);
+                    tmem_ld32(tmem + buf * BN + c * 64 + 32 + lane_off, v + 32);
+                    tmem_wait_ld();
+                    if (ep.bias) {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            float bv[8];
+                            load8_nc(ep.bias + col0 + c * 64 + q * 8, bv);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) v[q * 8 + j] += bv[j];
+                        }
+                    }
+                    uint8_t* box = sm.ostage[ew][nstore & 1];
+                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                    __syncwarp();
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        *reinterpret_cast<uint4*>(box + lane * 128 + ((q ^ (lane & 7)) << 4)) = pack8(v + q * 8);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (row0 < m) tma_store_2d(&tmO, smem_u32(box), col0 + c * 64, row0);   // no box starts past m
+                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&sm.acc_empty[buf]), 0));
+        }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();    // no CTA leaves while its peer's MMAs or arrivals may still touch it
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+    }
+}
+
+bool make_map(CUtensorMap* map, const void* base, int64_t rows, int cols, int64_t ld, int box_rows,
+              int box_cols = BK) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    cuuint32_t es[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int num_sms() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            n = 148;
+    }
+    return n;
+}
+
+template <int EPI>
+int launch(const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo, int64_t m, int n, int k,
+           const EpiArgs& ep, cudaStream_t s) {
+    const size_t smem = sizeof(Smem) + 1024;
+    static int max_pairs = 0;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (max_pairs == 0) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e == cudaSuccess) {
+            cfg.gridDim = dim3(2 * (num_sms() / 2));
+            e = cudaOccupancyMaxActiveClusters(&max_pairs, gemm_kernel<EPI>, &cfg);
+        }
+        if (e != cudaSuccess || max_pairs <= 0) {
+            max_pairs = 0;
+            record_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidConfiguration);
+            return VDIT_ERR_LAUNCH;
+        }
+    }
+    const int64_t ntiles = ((m + 2 * BM - 1) / (2 * BM)) * (n / BN);
+    cfg.gridDim = dim3((unsigned)(2 * std::min<int64_t>(ntiles, max_pairs)));
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<EPI>, ma, mw, mo, m, n, k, ep);
+    if (e != cudaSuccess) {
+        record_cuda_error(e);
+        return VDIT_ERR_LAUNCH;
+    }
+    count_launches(1);
+    return check_launch();
+}
+
+}  // namespace gemm
+
+int gemm_error_word(int clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_gemm_error, sizeof(int)) != cudaSuccess) return VDIT_ERR_LAUNCH;
+    if (clear) {
+        int z = 0;
+        if (cudaMemcpyToSymbol(g_gemm_error, &z, sizeof(int)) != cudaSuccess) return VDIT_ERR_LAUNCH;
+    }
+    return v;
+}
+
+}  // namespace vdit
+
+using namespace vdit;
+
+extern "C" int vdit_linear(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias, void* out,
+                           int64_t ldo, int64_t m, int32_t n, int32_t k, vdit_stream_t stream) {
+    using namespace vdit::gemm;
+    if (!a || !w || !out || m < 0 || n <= 0 || k <= 0) return VDIT_ERR_ARG;
+    if (n % BN || k % BK) return VDIT_ERR_UNSUPPORTED;
+    if (lda < k || ldw < k || ldo < n) return VDIT_ERR_ARG;
+    if (!aligned16(a) || !aligned16(w) || !aligned16(out) || (bias && !aligned16(bias)) || lda % 8 || ldw % 8 ||
+        ldo % 8)
+        return VDIT_ERR_ALIGN;
+    if (m == 0) return VDIT_OK;
+    if (m > (int64_t)INT32_MAX) return VDIT_ERR_UNSUPPORTED;
+    CUtensorMap ma, mw, mo;
+    if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, BNH) || !make_map(&mo, out, m, n, ldo, 32, 64))
+        return VDIT_ERR_DRIVER;
+    EpiArgs ep{static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out), ldo};
+    return launch<EPI_BIAS>(ma, mw, mo, m, n, k, ep, static_cast<cudaStream_t>(stream));
+}

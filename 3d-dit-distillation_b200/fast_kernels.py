@@ -286,6 +286,30 @@ def dense_sparse_conv3d(feat: torch.Tensor, weight_t_bf16: torch.Tensor, bias_fp
     return out
 
 
+# ----------------------------------------------------------------------------- linears
+
+def linear(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
+           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``F.linear(a, w, bias)`` for bf16 2D ``a`` [M, K] (row stride free) and a
+    contiguous bf16 weight [N, K] on the tcgen05 GEMM (N % 256 == 0, K % 64 == 0)."""
+    if a.dtype != BF16 or w.dtype != BF16 or a.dim() != 2 or w.dim() != 2 or a.shape[1] != w.shape[1]:
+        raise ValueError(f"linear: a {tuple(a.shape)} {a.dtype} and w {tuple(w.shape)} {w.dtype} "
+                         "must be 2D bf16 with the same K")
+    if a.stride(1) != 1 or w.stride(1) != 1:
+        raise ValueError("linear: a and w need unit column stride")
+    m, k = a.shape
+    n = w.shape[0]
+    if bias is not None and (bias.dtype != BF16 or bias.numel() != n or not bias.is_contiguous()):
+        raise ValueError(f"linear: bias must be a contiguous bf16 vector of {n}")
+    if out is None:
+        out = torch.empty(m, n, dtype=BF16, device=a.device)
+    elif out.dtype != BF16 or out.dim() != 2 or out.shape[0] < m or out.shape[1] < n or out.stride(1) != 1:
+        raise ValueError(f"linear: out must be a bf16 2D view of at least [{m}, {n}]")
+    check(lib().vdit_linear(ptr(a), a.stride(0), ptr(w), w.stride(0), ptr(bias), ptr(out), out.stride(0), m, n, k,
+                            _s(a)), "linear")
+    return out
+
+
 # ----------------------------------------------------------------------------- attention
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_q: Sequence[int], cu_k: Sequence[int],

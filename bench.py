@@ -279,6 +279,44 @@ def gate_add_bench(w, reps: int = 20):
     return {"kernel": "gate_add_modulate", "ms_per_launch": ms, "gbs": 4 * w.n * D * 2 / ms / 1e6}
 
 
+def gemm_bench(w, reps: int = 20):
+    """The block linears of the workload (M = N voxels or the L context rows, bf16
+    in/out, fp32 accumulation): the tcgen05 GEMM beside cuBLAS (``F.linear``), same
+    inputs, CUDA events.  FLOPs 2*M*K*Nout per launch."""
+    import torch.nn.functional as F
+    from vdit import fast_kernels as fk
+    D = w.arch.dim
+    F2 = 2 * w.arch.ffn_dim
+    shapes = [("to_qkv", w.n, D, 3 * D), ("to_out", w.n, D, D), ("ffn0", w.n, D, F2),
+              ("ffn1", w.n, F2 // 2, D), ("cond_to_qkv", w.ctx_tokens, D, 3 * D)]
+    g = torch.Generator(device="cuda").manual_seed(9)
+    s = torch.cuda.current_stream()
+    res = []
+    for name, m, k, n in shapes:
+        a = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+        wt = (0.02 * torch.randn(n, k, device="cuda", generator=g)).to(torch.bfloat16)
+        b = (0.02 * torch.randn(n, device="cuda", generator=g)).to(torch.bfloat16)
+        out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+        row = {"gemm": name, "m": m, "k": k, "n": n}
+        for impl, fn in (("tcgen05", lambda: fk.linear(a, wt, b, out=out)), ("cublas", lambda: F.linear(a, wt, b))):
+            for _ in range(3):
+                fn()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(s)
+            for _ in range(reps):
+                fn()
+            e1.record(s)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / reps
+            row[impl + "_ms"] = round(ms, 4)
+            row[impl + "_tflops"] = round(2 * m * k * n / ms / 1e9, 1)
+        ref = F.linear(a, wt, b).float()
+        row["rel_l2_vs_cublas"] = float((fk.linear(a, wt, b).float() - ref).norm() / ref.norm())
+        res.append(row)
+    return res
+
+
 def dense_conv_bench(reps: int = 5):
     """C3: dense 27-tap sparse conv, N=65536 voxels of a sphere shell (r=56) in 128^3,
     features [N,1536] bf16, weights [27,1536,1536], fp32 accumulation.  FLOPs are
@@ -354,7 +392,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="one warm-up sample, then one sample inside the NVTX range 'profile_step' (for ncu)")
-    ap.add_argument("--only", choices=["attention", "dwconv", "dense_conv", "qknorm", "gate_add", "graph"], default=None,
+    ap.add_argument("--only", choices=["attention", "dwconv", "dense_conv", "qknorm", "gate_add", "graph", "gemm"], default=None,
                     help="run only one kernel on the workload's shapes (small ncu case)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -384,6 +422,10 @@ def main():
         return
     if args.only == "gate_add":
         print(json.dumps(gate_add_bench(w)))
+        return
+    if args.only == "gemm":
+        for row in gemm_bench(w):
+            print(json.dumps(row))
         return
     if args.only == "graph":
         print(json.dumps(graph_bench(w)))

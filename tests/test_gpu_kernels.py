@@ -355,3 +355,34 @@ def test_dense_conv27_rejects_bad_shapes():
     with pytest.raises(RuntimeError, match="unsupported"):
         fk.dense_sparse_conv3d(f, torch.zeros(27, 256, 100, device=DEV, dtype=torch.bfloat16),
                                torch.zeros(256, device=DEV), [torch.zeros(10, 27, dtype=torch.int32, device=DEV)])
+
+
+# ----------------------------------------------------------------------------- block linears (tcgen05 GEMM)
+
+@pytest.mark.parametrize("m,k,n,bias,strided", [(1, 64, 256, True, False), (300, 1536, 512, True, False),
+                                                 (4101, 1536, 4608, True, False), (16384, 1536, 1536, False, False),
+                                                 (1000, 3840, 1536, True, True), (129, 128, 768, True, True)])
+def test_linear_matches_fp32(m, k, n, bias, strided):
+    g = torch.Generator(device=DEV).manual_seed(m + k + n)
+    a_full = torch.randn(m, k + (64 if strided else 0), device=DEV, generator=g).to(torch.bfloat16)
+    a = a_full[:, 16:16 + k] if strided else a_full             # row stride k + 64, 32-byte offset
+    w = (0.03 * torch.randn(n, k, device=DEV, generator=g)).to(torch.bfloat16)
+    b = (0.1 * torch.randn(n, device=DEV, generator=g)).to(torch.bfloat16) if bias else None
+    out_full = torch.full((m, n + (256 if strided else 0)), 7.0, device=DEV, dtype=torch.bfloat16)
+    out = out_full[:, :n]
+    fk.linear(a, w, b, out=out)
+    ref = a.float() @ w.float().t() + (b.float() if bias else 0.0)
+    assert rel(out, ref) < 5e-3                                  # bf16 output rounding
+    if strided:
+        assert bool((out_full[:, n:] == 7.0).all())              # columns past n untouched
+    cub = torch.nn.functional.linear(a, w, b)
+    assert rel(out, cub) < 5e-3
+
+
+def test_linear_rejects_bad_shapes():
+    a = torch.zeros(10, 100, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="unsupported"):
+        fk.linear(a, torch.zeros(256, 100, device=DEV, dtype=torch.bfloat16))
+    with pytest.raises(RuntimeError, match="unsupported"):
+        fk.linear(torch.zeros(10, 128, device=DEV, dtype=torch.bfloat16),
+                  torch.zeros(100, 128, device=DEV, dtype=torch.bfloat16))
