@@ -55,11 +55,23 @@ struct __align__(1024) Smem {
 
 // epilogue kinds
 constexpr int EPI_BIAS = 0;   // out = bf16(acc + bias)
+constexpr int EPI_QKV = 1;    // self-attention qkv: QK-RMSNorm + 3D RoPE, rows scattered to window order
+constexpr int kQkvHd = 128;   // head_dim of EPI_QKV: a 256-column tile holds two whole heads
+constexpr int kQkvM = kQkvHd / 6;   // RoPE frequencies per axis (x, y, z); channels 126, 127 pass
 
 struct EpiArgs {
     const __nv_bfloat16* bias;   // [N] or null
     __nv_bfloat16* out;
     int64_t ldo;
+    // EPI_QKV only
+    const float* q_scale;        // [D] RMSNorm scales of q and k (no +1)
+    const float* k_scale;
+    const float* cos_t;          // [res, kQkvM] RoPE table (staged into shared memory)
+    const float* sin_t;
+    const int4* coords;          // [M] (b, x, y, z) of each input row
+    const int64_t* dst_rows;     // [M] output row of each input row
+    int d;                       // heads * 128: columns of each of q, k, v
+    int res;
 };
 
 // Banded tile order: the pairs walk GM m-tiles x all n-tiles before the next band,
@@ -109,6 +121,14 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmO)) : "memory");
+    }
+    if (EPI == EPI_QKV) {   // RoPE tables into the staging area (this epilogue stores from registers)
+        float* tab = reinterpret_cast<float*>(&sm.ostage[0][0][0]);
+        const int nt = ep.res * kQkvM;
+        for (int i = threadIdx.x; i < nt; i += THREADS) {
+            tab[i] = __ldg(ep.cos_t + i);
+            tab[nt + i] = __ldg(ep.sin_t + i);
+        }
     }
     if (warp == 1) {   // both CTAs of the pair allocate together (same warp, same slot offset)
         asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&sm.tmem_slot)));
@@ -224,11 +244,77 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
                     }
                 }
             }
+            if (EPI == EPI_QKV) {
+                // one thread per row: the row's two heads of q, k or v; q/k get
+                // RoPE3D(bf16(RMSNorm(x)) * scale), exactly as the separate pass computes from
+                // the bf16 GEMM output; the row goes to out[dst_rows[row]]
+                const int64_t row = (int64_t)row0 + lane;
+                const bool live = row < m;
+                int64_t orow = 0;
+                int tr[3] = {0, 0, 0};
+                if (live) {
+                    orow = __ldg(ep.dst_rows + row);
+                    const int4 c = __ldg(ep.coords + row);
+                    tr[0] = min(max(c.y, 0), ep.res - 1) * kQkvM;
+                    tr[1] = min(max(c.z, 0), ep.res - 1) * kQkvM;
+                    tr[2] = min(max(c.w, 0), ep.res - 1) * kQkvM;
+                }
+                const float* cs_s = reinterpret_cast<const float*>(&sm.ostage[0][0][0]);
+                const float* sn_s = cs_s + ep.res * kQkvM;
+#pragma unroll 1
+                for (int hh = 0; hh < BN / kQkvHd; ++hh) {
+                    const int col = col0 + hh * kQkvHd;
+                    const int section = col / ep.d;                 // 0 q, 1 k, 2 v
+                    float x[kQkvHd];
+#pragma unroll
+                    for (int cc = 0; cc < kQkvHd / 32; ++cc)
+                        tmem_ld32(tmem + buf * BN + hh * kQkvHd + cc * 32 + lane_off, x + cc * 32);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int q = 0; q < kQkvHd / 8; ++q) {
+                        float bv[8];
+                        load8_nc(ep.bias + col + q * 8, bv);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) x[q * 8 + j] = bf2f(f2bf(x[q * 8 + j] + bv[j]));
+                    }
+                    if (section < 2) {
+                        float ss[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                        for (int e = 0; e < kQkvHd; ++e) ss[e & 3] += x[e] * x[e];
+                        const float rr = rsqrtf(((ss[0] + ss[1]) + (ss[2] + ss[3])) / (float)kQkvHd + 1e-6f);
+                        const float* sc = (section == 0 ? ep.q_scale : ep.k_scale) + (col - section * ep.d);
+#pragma unroll
+                        for (int q = 0; q < kQkvHd / 4; ++q) {
+                            const float4 s4 = __ldg(reinterpret_cast<const float4*>(sc) + q);
+                            x[4 * q + 0] = bf2f(f2bf(x[4 * q + 0] * rr)) * s4.x;
+                            x[4 * q + 1] = bf2f(f2bf(x[4 * q + 1] * rr)) * s4.y;
+                            x[4 * q + 2] = bf2f(f2bf(x[4 * q + 2] * rr)) * s4.z;
+                            x[4 * q + 3] = bf2f(f2bf(x[4 * q + 3] * rr)) * s4.w;
+                        }
+#pragma unroll
+                        for (int g = 0; g < 3; ++g) {
+#pragma unroll
+                            for (int f = 0; f < kQkvM; ++f) {
+                                const int e0 = g * 2 * kQkvM + f, e1 = e0 + kQkvM;
+                                const float c = cs_s[tr[g] + f], sn = sn_s[tr[g] + f];
+                                const float a = x[e0], b = x[e1];
+                                x[e0] = a * c - b * sn;
+                                x[e1] = b * c + a * sn;
+                            }
+                        }
+                    }
+                    if (live) {
+                        __nv_bfloat16* dst = ep.out + orow * ep.ldo + col;
+#pragma unroll
+                        for (int q = 0; q < kQkvHd / 8; ++q) *reinterpret_cast<uint4*>(dst + q * 8) = pack8(x + q * 8);
+                    }
+                }
+            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&sm.acc_empty[buf]), 0));
         }
-        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        if (EPI == EPI_BIAS && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
 
     tc_fence_before();
@@ -334,4 +420,31 @@ extern "C" int vdit_linear(const void* a, int64_t lda, const void* w, int64_t ld
         return VDIT_ERR_DRIVER;
     EpiArgs ep{static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out), ldo};
     return launch<EPI_BIAS>(ma, mw, mo, m, n, k, ep, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int vdit_linear_qkv_rope3d(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias,
+                                      const float* q_scale, const float* k_scale, const float* cos_t,
+                                      const float* sin_t, int32_t res, const int32_t* coords,
+                                      const int64_t* dst_rows, void* out, int64_t ldo, int64_t m, int32_t heads,
+                                      int32_t head_dim, int32_t k, vdit_stream_t stream) {
+    using namespace vdit::gemm;
+    if (!a || !w || !bias || !q_scale || !k_scale || !cos_t || !sin_t || !coords || !dst_rows || !out || m < 0 ||
+        heads <= 0 || k <= 0 || res <= 0)
+        return VDIT_ERR_ARG;
+    const int64_t n64 = 3LL * heads * head_dim;
+    if (head_dim != kQkvHd || n64 % BN || k % BK || n64 > INT32_MAX) return VDIT_ERR_UNSUPPORTED;
+    if ((int64_t)res * kQkvM * 2 * 4 > (int64_t)sizeof(Smem::ostage)) return VDIT_ERR_UNSUPPORTED;
+    const int n = (int)n64;
+    if (lda < k || ldw < k || ldo < n) return VDIT_ERR_ARG;
+    if (!aligned16(a) || !aligned16(w) || !aligned16(out) || !aligned16(bias) || !aligned16(q_scale) ||
+        !aligned16(k_scale) || !aligned16(coords) || lda % 8 || ldw % 8 || ldo % 8)
+        return VDIT_ERR_ALIGN;
+    if (m == 0) return VDIT_OK;
+    if (m > (int64_t)INT32_MAX) return VDIT_ERR_UNSUPPORTED;
+    CUtensorMap ma, mw, mo;
+    if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, BNH) || !make_map(&mo, out, m, n, ldo, 32, 64))
+        return VDIT_ERR_DRIVER;
+    EpiArgs ep{static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out), ldo, q_scale, k_scale,
+               cos_t, sin_t, reinterpret_cast<const int4*>(coords), dst_rows, heads * head_dim, res};
+    return launch<EPI_QKV>(ma, mw, mo, m, n, k, ep, static_cast<cudaStream_t>(stream));
 }

@@ -100,6 +100,9 @@ class OptimizedLatDitRunner:
         # the 1-token NFE of a guided step runs on its own stream beside the conditional one
         self.overlap_branches = True
         self._neg_stream: Optional[torch.cuda.Stream] = None
+        # the self-attention to_qkv GEMM runs QK-norm, RoPE3D and the window-order scatter
+        # in its epilogue (tcgen05 GEMM) where the head layout allows (head_dim 128, even heads)
+        self.fused_qkv = self.head_dim == 128 and (3 * self.dim) % 256 == 0
         # CUDA-graph replay of the sampler (per voxel count, context length and schedule)
         self.cuda_graph = bool(cuda_graph)
         self._graphs: "OrderedDict[tuple, _SampleGraph]" = OrderedDict()
@@ -255,10 +258,14 @@ class OptimizedLatDitRunner:
         """Window self-attention in Hilbert order orders[b % 4]; returns to_out(o) [N, D]."""
         w, H, HD = self.blocks[b], self.num_heads, self.head_dim
         D = self.dim
-        qkv = F.linear(h_mod, w["to_qkv"], w["to_qkv_b"])
-        fwd, _bwd, cu, _ = geom["order_caches"][b % len(geom["order_caches"])]
-        qkv_s = fk.fused_qknorm_rope3d_gather(qkv, w["qs"], w["ks"], self.cos3, self.sin3, geom["h_coords"], fwd, H,
-                                              HD)
+        fwd, bwd, cu, _ = geom["order_caches"][b % len(geom["order_caches"])]
+        if self.fused_qkv:
+            qkv_s = fk.linear_qkv_rope3d(h_mod, w["to_qkv"], w["to_qkv_b"], w["qs"], w["ks"], self.cos3, self.sin3,
+                                         geom["h_coords"], bwd, H, HD)
+        else:
+            qkv = F.linear(h_mod, w["to_qkv"], w["to_qkv_b"])
+            qkv_s = fk.fused_qknorm_rope3d_gather(qkv, w["qs"], w["ks"], self.cos3, self.sin3, geom["h_coords"], fwd,
+                                                  H, HD)
         timer = self.attention_timer
         if timer is not None:
             e0 = torch.cuda.Event(enable_timing=True)

@@ -310,6 +310,34 @@ def linear(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None
     return out
 
 
+def linear_qkv_rope3d(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, q_scale: torch.Tensor,
+                      k_scale: torch.Tensor, cos_t: torch.Tensor, sin_t: torch.Tensor, h_coords: torch.Tensor,
+                      bwd_idx: torch.Tensor, heads: int, head_dim: int,
+                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``fused_qknorm_rope3d_gather(F.linear(a, w, bias), ..., fwd)`` in one tcgen05 GEMM:
+    the QK-norm / RoPE3D pass runs in the GEMM epilogue and input row r is written to
+    row ``bwd_idx[r]`` (``bwd_idx`` = the inverse of the window order ``fwd``)."""
+    m, k = a.shape
+    n = 3 * heads * head_dim
+    if a.dtype != BF16 or w.dtype != BF16 or bias.dtype != BF16 or a.stride(1) != 1 or w.shape != (n, k) \
+            or not w.is_contiguous() or bias.numel() != n:
+        raise ValueError("linear_qkv_rope3d: bf16 a [M, K] (unit column stride), w [3*H*HD, K], bias [3*H*HD]")
+    if h_coords.dtype != torch.int32 or h_coords.shape != (m, 4) or not h_coords.is_contiguous():
+        raise ValueError("linear_qkv_rope3d: h_coords must be contiguous int32 [M, 4]")
+    if bwd_idx.dtype != torch.int64 or bwd_idx.numel() != m:
+        raise ValueError("linear_qkv_rope3d: bwd_idx must be int64 [M]")
+    for t in (q_scale, k_scale, cos_t, sin_t):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError("linear_qkv_rope3d: scales and RoPE tables must be contiguous fp32")
+    if out is None:
+        out = torch.empty(m, n, dtype=BF16, device=a.device)
+    check(lib().vdit_linear_qkv_rope3d(ptr(a), a.stride(0), ptr(w), w.stride(0), ptr(bias), ptr(q_scale),
+                                       ptr(k_scale), ptr(cos_t), ptr(sin_t), cos_t.shape[0], ptr(h_coords),
+                                       ptr(bwd_idx), ptr(out), out.stride(0), m, heads, head_dim, k, _s(a)),
+          "linear_qkv_rope3d")
+    return out
+
+
 # ----------------------------------------------------------------------------- attention
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_q: Sequence[int], cu_k: Sequence[int],

@@ -225,6 +225,20 @@ int vdit_dense_conv27(const void* f, int64_t n, int32_t cin, int32_t cout, const
 int vdit_linear(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias, void* out,
                 int64_t ldo, int64_t m, int32_t n, int32_t k, vdit_stream_t stream);
 
+/* The self-attention to_qkv linear with the QK-norm / RoPE / window-order pass fused
+ * into its epilogue: for input row r, out[dst_rows[r], :] = the three [heads, 128]
+ * sections of bf16(a[r] . w^T + bias) with q and k replaced by
+ * RoPE3D(bf16(RMSNorm(.)) * scale) at coords[r] = (b, x, y, z): the result of
+ * vdit_linear followed by vdit_qknorm_rope3d_gather with fwd = the inverse of
+ * dst_rows (lib/fast_flow.py:1450-1464, lib/fast_kernels.py:1476-1535).
+ * head_dim == 128 and 3*heads*128 % 256 == 0 (even heads); cos_t/sin_t [res, 21]
+ * fp32 (res <= 195); q_scale/k_scale [heads*128] fp32; coords int32 [m, 4];
+ * dst_rows int64 [m], a permutation of 0..m-1. */
+int vdit_linear_qkv_rope3d(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias,
+                           const float* q_scale, const float* k_scale, const float* cos_t, const float* sin_t,
+                           int32_t res, const int32_t* coords, const int64_t* dst_rows, void* out, int64_t ldo,
+                           int64_t m, int32_t heads, int32_t head_dim, int32_t k, vdit_stream_t stream);
+
 /* ------------------------------------------------------------------ sampler glue */
 /* dst[j,:] = src[idx[j],:] for fp32 rows of width c (noise[perm], lib/fast_flow.py:2576). */
 int vdit_gather_rows_f32(const float* src, const int64_t* idx, int64_t n, int32_t c, float* dst,

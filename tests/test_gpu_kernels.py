@@ -386,3 +386,48 @@ def test_linear_rejects_bad_shapes():
     with pytest.raises(RuntimeError, match="unsupported"):
         fk.linear(torch.zeros(10, 128, device=DEV, dtype=torch.bfloat16),
                   torch.zeros(100, 128, device=DEV, dtype=torch.bfloat16))
+
+
+@pytest.mark.parametrize("n,heads,res", [(3000, 12, 128), (16384, 12, 64), (300, 2, 64)])
+def test_linear_qkv_rope3d_matches_two_pass(n, heads, res):
+    """The fused epilogue against the two-pass path (GEMM, then the QK-norm / RoPE /
+    gather kernel) and the fp32 oracle; rows land at bwd[r]."""
+    hd, K = 128, 1536
+    vox = unique_cells(n, res, n + heads)
+    _, _, hc = fk.lex_perm(torch.from_numpy(vox).to(DEV))
+    g = torch.Generator(device=DEV).manual_seed(n + res)
+    D = heads * hd
+    a = torch.randn(n, K, device=DEV, generator=g).to(torch.bfloat16)
+    w = (0.03 * torch.randn(3 * D, K, device=DEV, generator=g)).to(torch.bfloat16)
+    b = (0.1 * torch.randn(3 * D, device=DEV, generator=g)).to(torch.bfloat16)
+    qs = 1 + 0.1 * torch.randn(D, device=DEV, generator=g)
+    ks = 1 + 0.1 * torch.randn(D, device=DEV, generator=g)
+    fwd = torch.randperm(n, device=DEV, generator=g)
+    bwd = torch.empty_like(fwd)
+    bwd[fwd] = torch.arange(n, device=DEV)
+    cos, sin = fk.precompute_rope_3d_table(res, 128.0, hd, device=DEV)
+    fused = fk.linear_qkv_rope3d(a, w, b, qs, ks, cos, sin, hc, bwd, heads, hd)
+    two = fk.fused_qknorm_rope3d_gather(fk.linear(a, w, b), qs, ks, cos, sin, hc, fwd, heads, hd)
+    d = (fused.float() - two.float()).abs()
+    # same bf16 GEMM output; only the order of the RMS sum differs (a rare 1-ulp bf16 flip)
+    assert float((d > 0).float().mean()) < 1e-3 and float(d.max()) <= 0.0625
+    assert torch.equal(fused[:, 2 * D:], two[:, 2 * D:])          # v rows: the bf16 GEMM output, moved
+    src = (a.float() @ w.float().t() + b.float())[fwd].view(n, 3, heads, hd).cpu()
+    pos = ((hc.float()[fwd][:, 1:] + 0.5) / res * 2 - 1).cpu()
+    q = om.rope_nd(om.rms_norm(src[:, 0]) * qs.view(heads, hd).cpu(), pos, 128.0)
+    fv = fused.view(n, 3, heads, hd)
+    assert rel(fv[:, 0], q) < 1e-2
+
+
+def test_linear_qkv_rope3d_rejects_odd_shapes():
+    n, K = 64, 128
+    a = torch.zeros(n, K, device=DEV, dtype=torch.bfloat16)
+    hc = torch.zeros(n, 4, device=DEV, dtype=torch.int32)
+    bwd = torch.arange(n, device=DEV)
+    cos, sin = fk.precompute_rope_3d_table(64, 128.0, 128, device=DEV)
+    for heads, hd in ((3, 128), (2, 96)):                          # 3*H*128 % 256 != 0; head_dim 96
+        D = heads * hd
+        with pytest.raises(RuntimeError, match="unsupported"):
+            fk.linear_qkv_rope3d(a, torch.zeros(3 * D, K, device=DEV, dtype=torch.bfloat16),
+                                 torch.zeros(3 * D, device=DEV, dtype=torch.bfloat16), torch.ones(D, device=DEV),
+                                 torch.ones(D, device=DEV), cos, sin, hc, bwd, heads, hd)
