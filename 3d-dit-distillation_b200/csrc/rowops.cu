@@ -124,9 +124,10 @@ __global__ void __launch_bounds__(256) gate_add_modulate_kernel(
 // The same operation as gate_add_modulate_kernel from persistent CTAs: one CTA
 // per SM stages g, s1, sh in shared memory once, and each warp walks rows with
 // a stride, bulk-copying the next row's x and h into its second buffer while
-// the current row is reduced and written.  Arithmetic is identical to the
-// one-row-per-warp kernel.  Waits on the bulk copies are bounded; a timeout
-// sets the row kernels' error word.
+// the current row is reduced and written.  With h == nullptr the kernel is the
+// plain modulation (modulate_kernel): only x is copied and x is not written.
+// Arithmetic is identical to the one-row-per-warp kernels.  Waits on the bulk
+// copies are bounded; a timeout sets the row kernels' error word.
 constexpr int kGaMaxWarps = 16;
 constexpr int kErrRowTimeout = 0x524f;   // "RO": a bounded wait of a row kernel ran out
 
@@ -145,6 +146,7 @@ __global__ void __launch_bounds__(kGaMaxWarps * 32, 1) gate_add_modulate_staged_
     const int nwarps = blockDim.x >> 5;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool mod = mod_out != nullptr;
+    const bool add = h != nullptr;
     float* pg = reinterpret_cast<float*>(smem);
     float* ps1 = pg + d;
     float* psh = ps1 + d;
@@ -153,7 +155,7 @@ __global__ void __launch_bounds__(kGaMaxWarps * 32, 1) gate_add_modulate_staged_
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)12 * d + (size_t)nwarps * 4 * row_bytes) + warp * 2;
     const uint32_t bar_u[2] = {tc::smem_u32(bars), tc::smem_u32(bars + 1)};
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
-        pg[i] = g[i];
+        if (add) pg[i] = g[i];
         if (mod) {
             ps1[i] = s1[i];
             psh[i] = sh[i];
@@ -171,9 +173,9 @@ __global__ void __launch_bounds__(kGaMaxWarps * 32, 1) gate_add_modulate_staged_
     const int64_t stride = (int64_t)gridDim.x * nwarps;
     auto issue = [&](int64_t row, int b) {
         const uint32_t dst = tc::smem_u32(wbuf + b * 2 * row_bytes);
-        tc::mbar_expect_tx(bar_u[b], 2 * row_bytes);
+        tc::mbar_expect_tx(bar_u[b], (add ? 2 : 1) * row_bytes);
         bulk_load(dst, x + row * d, row_bytes, bar_u[b]);
-        bulk_load(dst + row_bytes, h + row * h_stride, row_bytes, bar_u[b]);
+        if (add) bulk_load(dst + row_bytes, h + row * h_stride, row_bytes, bar_u[b]);
     };
     int64_t row = (int64_t)blockIdx.x * nwarps + warp;
     if (lane == 0 && row < m) issue(row, 0);
@@ -189,10 +191,13 @@ __global__ void __launch_bounds__(kGaMaxWarps * 32, 1) gate_add_modulate_staged_
         const __nv_bfloat16* hs = xs + d;
         __nv_bfloat16* xr = x + row * d;
         RowRegs r;
+        if (!add) {
+            row_load(xs, nvec, lane, r);
+        }
 #pragma unroll
         for (int i = 0; i < kMaxVec; ++i) {
             const int vi = lane + 32 * i;
-            if (vi >= nvec) continue;
+            if (!add || vi >= nvec) continue;
             float xv[8], hv[8];
             load8(xs + vi * 8, xv);
             load8(hs + vi * 8, hv);
@@ -597,6 +602,10 @@ extern "C" int vdit_modulate(const void* x, int64_t m, int32_t d, const float* s
     if (m < 0 || !row_width_ok(d) || !x || !s1 || !sh || !out) return VDIT_ERR_ARG;
     if (!aligned16(x) || !aligned16(out) || !aligned16(s1) || !aligned16(sh)) return VDIT_ERR_ALIGN;
     if (m == 0) return VDIT_OK;
+    if (m >= 4096)       // persistent CTAs with bulk-copied rows (the staged kernel without its gate-add)
+        return launch_gate_add_staged(const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(x)), nullptr, 0, m,
+                                      d, nullptr, s1, sh, static_cast<__nv_bfloat16*>(out),
+                                      static_cast<cudaStream_t>(stream));
     modulate_kernel<<<blocks_for(m, kRowWarps), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16*>(x), m, d, s1, sh, static_cast<__nv_bfloat16*>(out));
     count_launches(1);

@@ -314,6 +314,36 @@ def gemm_bench(w, reps: int = 20):
         ref = F.linear(a, wt, b).float()
         row["rel_l2_vs_cublas"] = float((fk.linear(a, wt, b).float() - ref).norm() / ref.norm())
         res.append(row)
+    # the self-attention qkv with QK-norm, RoPE3D and the window-order scatter in the epilogue,
+    # against cuBLAS followed by the separate QK-norm / RoPE / gather pass
+    from vdit.workloads import shell_voxels
+    H, HD = w.arch.heads, w.arch.head_dim
+    vox = torch.from_numpy(shell_voxels(w.n, w.grid, w.radius, 0)).cuda()
+    _, _, hc = fk.lex_perm(vox)
+    fwd, bwd = fk.hilbert4_orders(hc, w.grid)
+    fwd, bwd = fwd[0].contiguous(), bwd[0].contiguous()
+    cos, sin = fk.precompute_rope_3d_table(w.grid, 128.0, HD, device="cuda")
+    a = torch.randn(w.n, D, device="cuda", generator=g).to(torch.bfloat16)
+    wt = (0.02 * torch.randn(3 * D, D, device="cuda", generator=g)).to(torch.bfloat16)
+    b = (0.02 * torch.randn(3 * D, device="cuda", generator=g)).to(torch.bfloat16)
+    qs, ks = 1 + 0.1 * torch.randn(D, device="cuda", generator=g), 1 + 0.1 * torch.randn(D, device="cuda", generator=g)
+    out = torch.empty(w.n, 3 * D, device="cuda", dtype=torch.bfloat16)
+    row = {"gemm": "to_qkv + QK-norm/RoPE3D/window scatter", "m": w.n, "k": D, "n": 3 * D}
+    impls = (("fused_epilogue", lambda: fk.linear_qkv_rope3d(a, wt, b, qs, ks, cos, sin, hc, bwd, H, HD, out=out)),
+             ("cublas_then_qknorm", lambda: fk.fused_qknorm_rope3d_gather(F.linear(a, wt, b), qs, ks, cos, sin, hc,
+                                                                         fwd, H, HD, out=out)))
+    for impl, fn in impls:
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(reps):
+            fn()
+        e1.record(s)
+        torch.cuda.synchronize()
+        row[impl + "_ms"] = round(e0.elapsed_time(e1) / reps, 4)
+    res.append(row)
     return res
 
 

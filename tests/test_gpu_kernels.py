@@ -129,6 +129,10 @@ def test_gate_add_staged_matches_rowwise(m, d, stride_h):
     xc = x.clone()
     fk.fast_gate_add_and_modulate(xc, h, gt, None, None)
     assert torch.equal(xc, xa)
+    # plain modulation: the staged kernel without its gate-add against the row-per-warp kernel
+    mod_s = fk.fast_modulate(x, None, s1, sh)
+    mod_r = torch.cat([fk.fast_modulate(x[i:i + 2048], None, s1, sh) for i in range(0, m, 2048)])
+    assert torch.equal(mod_s, mod_r)
 
 
 def test_out_modulate_unpatchify():
