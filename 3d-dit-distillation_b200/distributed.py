@@ -1,5 +1,6 @@
 """Multi-GPU plumbing of the sampler: one process per GPU, samples sharded
-across ranks, latents gathered to rank 0.
+across ranks, latents gathered to rank 0; for fewer samples than GPUs, the two
+branches of a guided step split over two ranks (``branch_split_steps``).
 
 Samples are independent (each owns its geometry and its 7 NFEs), so the forward
 has no collective; the only exchange is the end-of-run gather of the
@@ -68,3 +69,33 @@ def gather_latents(latents: Sequence[torch.Tensor], rank: int, world: int,
         for i in range(k):
             res.append(outs[r][i, : int(all_sizes[r][i])])
     return res
+
+
+def branch_split_steps(xt: torch.Tensor, tl: Sequence[float], guided: Sequence[bool], g_scale: float, nfe, cfg_euler,
+                       group=None) -> torch.Tensor:
+    """The sampler's Euler + CFG loop for ONE sample on TWO ranks, for runs with fewer
+    samples than GPUs (the reference runs both branches of a guided step on one GPU,
+    ``lib/fast_flow.py:2836,2887,3288``).
+
+    In a guided step, group rank 0 runs the conditional NFE and rank 1 the unconditional
+    one at the same time.  The two ``[N, C]`` velocities are all-gathered, and both ranks
+    apply the same CFG + Euler update, so ``xt`` stays identical on both.  In an unguided
+    step rank 0 runs the NFE and broadcasts its velocity.
+    ``nfe(x, t, uncond) -> v`` and ``cfg_euler(x, v, v_uncond or None, g, dt)`` (in place)
+    are the caller's.  Every rank takes the same collective steps in the same order."""
+    if dist.get_world_size(group) != 2:
+        raise ValueError("the branch split runs on exactly two ranks")
+    rank = dist.get_rank(group)
+    src = dist.get_global_rank(group, 0) if group is not None else 0
+    for i in range(len(guided)):
+        dt = float(tl[i]) - float(tl[i + 1])
+        if guided[i] and g_scale > 0:
+            v_mine = nfe(xt, tl[i], rank == 1).contiguous()
+            vs = [torch.empty_like(v_mine) for _ in range(2)]
+            dist.all_gather(vs, v_mine, group=group)
+            cfg_euler(xt, vs[0], vs[1], g_scale, dt)
+        else:
+            v = nfe(xt, tl[i], False).contiguous() if rank == 0 else torch.empty_like(xt)
+            dist.broadcast(v, src=src, group=group)
+            cfg_euler(xt, v, None, g_scale, dt)
+    return xt

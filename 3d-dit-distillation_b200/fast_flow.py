@@ -526,17 +526,7 @@ class OptimizedLatDitRunner:
         if noise is None:
             noise = torch.randn(N, self.latent_dim, dtype=F32, device=self.device, generator=generator)
         noise = noise.to(self.device, F32)
-        sc = self.solver_config
-        g_scale, steps_ovr, r_ovr, cr_ovr = sc.guidance_scale, None, None, None
-        if sampling is not None:
-            g_scale = float(sampling.guidance_scale)
-            r_ovr = float(sampling.rescale_t)
-            cr_ovr = tuple(float(v) for v in sampling.cfg_range)
-            if sampling.num_inference_steps != 50:
-                steps_ovr = int(sampling.num_inference_steps)
-        t_seq, guided, _ = build_schedule(sc, steps_ovr, r_ovr, cr_ovr)
-        tl = [float(t) for t in t_seq.tolist()]
-        guided = [bool(g) for g in guided]
+        tl, guided, g_scale = self._schedule(sampling)
         use_graph = self.cuda_graph if cuda_graph is None else bool(cuda_graph)
         if not use_graph:
             return self._sample_steps(geom, context, noise, tl, guided, g_scale)
@@ -551,6 +541,51 @@ class OptimizedLatDitRunner:
             entry.noise.copy_(noise)
         entry.graph.replay()
         return entry.out.clone()
+
+    def _schedule(self, sampling: Optional[FlowMatchSamplingParams]):
+        """(t nodes, guided flags, guidance scale) of the solver config with the call's overrides."""
+        sc = self.solver_config
+        g_scale, steps_ovr, r_ovr, cr_ovr = sc.guidance_scale, None, None, None
+        if sampling is not None:
+            g_scale = float(sampling.guidance_scale)
+            r_ovr = float(sampling.rescale_t)
+            cr_ovr = tuple(float(v) for v in sampling.cfg_range)
+            if sampling.num_inference_steps != 50:
+                steps_ovr = int(sampling.num_inference_steps)
+        t_seq, guided, _ = build_schedule(sc, steps_ovr, r_ovr, cr_ovr)
+        return [float(t) for t in t_seq.tolist()], [bool(g) for g in guided], g_scale
+
+    @torch.no_grad()
+    def sample_branch_split(self, vox: torch.Tensor, context: torch.Tensor, *, group=None,
+                            sampling: Optional[FlowMatchSamplingParams] = None,
+                            generator: Optional[torch.Generator] = None,
+                            noise: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One sample on two GPUs (one process each, a two-rank NCCL ``group``; the default
+        group when None): in every guided step the conditional NFE runs on group rank 0 and
+        the exact 1-token NFE on rank 1 at the same time, and the two velocities are
+        exchanged before the shared CFG + Euler update.  Both ranks pass the same voxels and
+        context; the noise is rank 0's (``noise`` or a draw from ``generator``), broadcast.
+        Both ranks return the same latents ([N, 16] fp32, input voxel order)."""
+        import torch.distributed as dist
+        from . import distributed as vd
+        geom = self._prepare_sample_geometry([vox], context)
+        N = geom["N"]
+        rank = dist.get_rank(group)
+        if rank == 0:
+            noise = (torch.randn(N, self.latent_dim, dtype=F32, device=self.device, generator=generator)
+                     if noise is None else noise.to(self.device, F32).contiguous())
+        else:
+            noise = torch.empty(N, self.latent_dim, dtype=F32, device=self.device)
+        dist.broadcast(noise, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+        tl, guided, g_scale = self._schedule(sampling)
+        xt = fk.gather_rows_f32(noise, geom["perm"])
+
+        def nfe(x, t, uncond):
+            return self.forward_flow_fast(x, t, context, None, geom, uncond=uncond)
+
+        vd.branch_split_steps(xt, tl, guided, g_scale, nfe, fk.cfg_euler_, group)
+        self._b0_share = None
+        return fk.unpermute_denorm(xt, geom["up_widx"], self._denorm_scale, self._denorm_shift)
 
     def _sample_steps(self, geom: Dict[str, Any], context: torch.Tensor, noise: torch.Tensor, tl: List[float],
                       guided: List[bool], g_scale: float) -> torch.Tensor:

@@ -377,6 +377,51 @@ def dense_conv_bench(reps: int = 5):
             "tflops_nnz": 2.0 * nnz * cin * cout / ms / 1e9, "tflops_dense27": 2.0 * 27 * n * cin * cout / ms / 1e9}
 
 
+def branch_split_bench(w, reps: int = 3):
+    """One C4 sample on two GPUs (torchrun, two ranks): the branch split (conditional NFE on
+    rank 0, exact 1-token NFE on rank 1, velocities exchanged over NCCL in every guided
+    step) against the same sample on rank 0 alone.  Latency per sample from CUDA events,
+    max over the two ranks."""
+    import torch.distributed as dist
+    from vdit.fast_flow import OptimizedLatDitRunner
+    from vdit.fast_sampler import SolverConfig
+    from vdit.model import LatDitModel
+    rank = dist.get_rank()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    model = LatDitModel.random(w.arch, seed=0, device=dev)
+    solver = SolverConfig(num_inference_steps=4, n_guided_steps=3, n_unguided_steps=1, guidance_scale=w.guidance)
+    runner = OptimizedLatDitRunner(model, solver, device=dev)
+    inp = w.inputs(seed=100, device=dev)                 # the same sample on both ranks
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    s = torch.cuda.current_stream()
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        tot = 0.0
+        for _ in range(reps):
+            _l2_flush(flush)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            fn()
+            e1.record(s)
+            torch.cuda.synchronize()
+            tot += e0.elapsed_time(e1)
+        t = torch.tensor([tot / reps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    split_ms = timed(lambda: runner.sample_branch_split(inp["vox"], inp["context"], noise=inp["noise"]))
+    one = runner.sample_with_context(inp["vox"], inp["context"], noise=inp["noise"])
+    two = runner.sample_branch_split(inp["vox"], inp["context"], noise=inp["noise"])
+    same = float((one - two).float().norm() / one.float().norm())
+    one_ms = timed(lambda: runner.sample_with_context(inp["vox"], inp["context"], noise=inp["noise"])
+                   if rank == 0 else None)
+    return {"mode": "branch_split", "n_gpus": 2, "voxels": w.n, "split_ms_per_sample": split_ms,
+            "one_gpu_ms_per_sample": one_ms, "speedup": one_ms / split_ms, "rel_l2_split_vs_one_gpu": same}
+
+
 def graph_bench(w, reps: int = 5):
     """Sample latency, eager vs CUDA-graph replay, on the workload's model at N = 4632
     (the size of the smallest public-test voxel set) and at the workload's N."""
@@ -422,7 +467,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="one warm-up sample, then one sample inside the NVTX range 'profile_step' (for ncu)")
-    ap.add_argument("--only", choices=["attention", "dwconv", "dense_conv", "qknorm", "gate_add", "graph", "gemm"], default=None,
+    ap.add_argument("--only", choices=["attention", "dwconv", "dense_conv", "qknorm", "gate_add", "graph", "gemm", "branch_split"], default=None,
                     help="run only one kernel on the workload's shapes (small ncu case)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -452,6 +497,14 @@ def main():
         return
     if args.only == "gate_add":
         print(json.dumps(gate_add_bench(w)))
+        return
+    if args.only == "branch_split":
+        if ws != 2:
+            raise SystemExit("--only branch_split runs under torchrun with two ranks")
+        r = branch_split_bench(w)
+        if rank == 0:
+            print(json.dumps(r))
+        dist.destroy_process_group()
         return
     if args.only == "gemm":
         for row in gemm_bench(w):

@@ -90,3 +90,53 @@ def test_shard_samples_cover_all():
     for world in (1, 2, 4, 8):
         owned = sorted(i for r in range(world) for i in vd.shard_samples(16, r, world))
         assert owned == list(range(16))
+
+
+def _fake_nfe(calls):
+    def nfe(x, t, uncond):
+        calls.append((t, uncond))
+        return torch.sin(x * (1.0 + t)) + (0.25 * x if uncond else 0.0)
+    return nfe
+
+
+def _fake_cfg(x, v, vn, g, dt):
+    vv = v if vn is None else v + g * (v - vn)
+    x.sub_(dt * vv)
+
+
+TL, GUIDED, G = [1.0, 0.9, 0.75, 0.5, 0.0], [True, True, True, False], 3.0
+
+
+def _branch_worker(rank, world, port, q):
+    vd = _setup(rank, world, port)
+    r, w, _ = vd.init_from_env("gloo", timeout_s=30)
+    calls = []
+    x = torch.linspace(-1, 1, 64).view(4, 16).clone()
+    vd.branch_split_steps(x, TL, GUIDED, G, _fake_nfe(calls), _fake_cfg)
+    q.put((r, x.tolist(), calls))
+    import torch.distributed as dist
+    dist.destroy_process_group()
+
+
+def test_branch_split_matches_one_process():
+    """Two gloo ranks run the split loop with a stand-in NFE: rank 0 only the conditional
+    branch, rank 1 only the unconditional one (guided steps), and both end with the x of
+    the one-process loop, bit for bit."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_branch_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict((r, (x, calls)) for r, x, calls in (q.get(timeout=120), q.get(timeout=120)))
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    x = torch.linspace(-1, 1, 64).view(4, 16).clone()
+    nfe = _fake_nfe([])
+    for i, gd in enumerate(GUIDED):
+        v = nfe(x, TL[i], False)
+        _fake_cfg(x, v, nfe(x, TL[i], True) if gd else None, G, TL[i] - TL[i + 1])
+    assert torch.equal(torch.tensor(res[0][0]), x) and torch.equal(torch.tensor(res[1][0]), x)
+    assert res[0][1] == [(1.0, False), (0.9, False), (0.75, False), (0.5, False)]
+    assert res[1][1] == [(1.0, True), (0.9, True), (0.75, True)]
