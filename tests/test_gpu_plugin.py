@@ -85,3 +85,26 @@ def test_runs_are_deterministic():
     s1 = runner.sample_fast([vox], cond, noise=noise)[0]
     s2 = runner.sample_fast([vox], cond, noise=noise)[0]
     assert torch.equal(s1, s2)
+
+
+def test_generate_from_sample_cache(tmp_path):
+    """The on-disk sample format into the plugin: vox_idxi.npz + 4view_000_dinov3.npz (fp16
+    features mapped by image_map on the GPU), latents in the file's voxel order."""
+    from vdit import ingest
+    sol, p, cfg = small_solution(71)
+    d = tmp_path / "s0" / "cache"
+    d.mkdir(parents=True)
+    vox = shell_voxels(400, 64, 18.0, 72)
+    np.savez(d / "vox_idxi.npz", vox_idxi=vox)
+    g = np.random.default_rng(73)
+    np.savez(d / "4view_000_dinov3.npz", feats=g.standard_normal((1, 5 + 64, 1280)).astype(np.float16),
+             token=g.standard_normal((1, 1280)).astype(np.float16))
+    vl, cond = ingest.load_sample(tmp_path / "s0", pin_memory=True)
+    gen = torch.Generator(device=DEV).manual_seed(74)
+    out = sol.generate(vl, conditioning=cond, generator=gen)[0]
+    assert out.shape == (400, 16) and bool(torch.isfinite(out).all())
+    g2 = torch.Generator(device=DEV).manual_seed(74)
+    noise = torch.randn(400, 16, device=DEV, generator=g2).cpu()
+    ctx = torch.nn.functional.linear(cond.dino_features[0].float(), p["image_map.weight"], p["image_map.bias"])
+    ref = om.sample(p, cfg, vox, ctx, noise, guidance_scale=3.0, num_steps=4, n_guided=3)
+    assert rel(out, ref) < 2e-2
