@@ -36,17 +36,16 @@ namespace gemm {
 using namespace tc;
 
 constexpr int BM = 128;             // rows per CTA (256 per pair)
-constexpr int BN = 256;             // output columns per pair tile
-constexpr int BNH = BN / 2;         // weight rows staged per CTA
+constexpr int BN_FULL = 256;        // output columns per pair tile (192 for the head_dim-96 qkv)
 constexpr int BK = 64, STAGES = 6;
 constexpr int EPI_WARPS = 4;
 constexpr int THREADS = (2 + EPI_WARPS) * 32;
-constexpr uint32_t kStageBytes = (BM + BNH) * 128;   // per CTA and k-step
 constexpr int kErr = 0x474D;   // "GM": a bounded wait of the GEMM kernel ran out
 
+template <int BN>
 struct __align__(1024) Smem {
     uint8_t a[STAGES][BM * 128];
-    uint8_t b[STAGES][BNH * 128];
+    uint8_t b[STAGES][BN / 2 * 128];    // this CTA's half of the weight tile
     uint8_t ostage[EPI_WARPS][2][32 * 128];   // per epilogue warp: two 32-row x 64-column bf16 boxes
     uint64_t full[STAGES], empty[STAGES], acc_full[2], acc_empty[2];
     uint32_t tmem_slot;
@@ -55,9 +54,8 @@ struct __align__(1024) Smem {
 
 // epilogue kinds
 constexpr int EPI_BIAS = 0;   // out = bf16(acc + bias)
-constexpr int EPI_QKV = 1;    // self-attention qkv: QK-RMSNorm + 3D RoPE, rows scattered to window order
-constexpr int kQkvHd = 128;   // head_dim of EPI_QKV: a 256-column tile holds two whole heads
-constexpr int kQkvM = kQkvHd / 6;   // RoPE frequencies per axis (x, y, z); channels 126, 127 pass
+constexpr int EPI_QKV = 1;    // self-attention qkv: QK-RMSNorm + 3D RoPE, rows scattered to window order;
+                              // a pair tile holds two whole heads (BN = 2 * head_dim, 256 or 192)
 
 struct EpiArgs {
     const __nv_bfloat16* bias;   // [N] or null
@@ -66,7 +64,7 @@ struct EpiArgs {
     // EPI_QKV only
     const float* q_scale;        // [D] RMSNorm scales of q and k (no +1)
     const float* k_scale;
-    const float* cos_t;          // [res, kQkvM] RoPE table (staged into shared memory)
+    const float* cos_t;          // [res, head_dim / 6] RoPE table (staged into shared memory)
     const float* sin_t;
     const int4* coords;          // [M] (b, x, y, z) of each input row
     const int64_t* dst_rows;     // [M] output row of each input row
@@ -91,13 +89,17 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
                  : "memory");
 }
 
-template <int EPI>
+template <int EPI, int BN>
 __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                           const __grid_constant__ CUtensorMap tmW,
                                                           const __grid_constant__ CUtensorMap tmO, int64_t m, int n,
                                                           int k, const __grid_constant__ EpiArgs ep) {
     extern __shared__ uint8_t raw[];
-    Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    constexpr int BNH = BN / 2;                      // weight rows staged per CTA
+    constexpr uint32_t kStageBytes = (BM + BNH) * 128;   // per CTA and k-step
+    constexpr int kQkvHd = BN / 2;                   // EPI_QKV: head_dim (two heads per tile)
+    constexpr int kQkvM = kQkvHd / 6;                // RoPE frequencies per axis (x, y, z)
+    Smem<BN>& sm = *reinterpret_cast<Smem<BN>*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
@@ -349,10 +351,10 @@ int num_sms() {
     return n;
 }
 
-template <int EPI>
+template <int EPI, int BN>
 int launch(const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo, int64_t m, int n, int k,
            const EpiArgs& ep, cudaStream_t s) {
-    const size_t smem = sizeof(Smem) + 1024;
+    const size_t smem = sizeof(Smem<BN>) + 1024;
     static int max_pairs = 0;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -366,10 +368,10 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo, 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     if (max_pairs == 0) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e == cudaSuccess) {
             cfg.gridDim = dim3(2 * (num_sms() / 2));
-            e = cudaOccupancyMaxActiveClusters(&max_pairs, gemm_kernel<EPI>, &cfg);
+            e = cudaOccupancyMaxActiveClusters(&max_pairs, gemm_kernel<EPI, BN>, &cfg);
         }
         if (e != cudaSuccess || max_pairs <= 0) {
             max_pairs = 0;
@@ -379,7 +381,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo, 
     }
     const int64_t ntiles = ((m + 2 * BM - 1) / (2 * BM)) * (n / BN);
     cfg.gridDim = dim3((unsigned)(2 * std::min<int64_t>(ntiles, max_pairs)));
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<EPI>, ma, mw, mo, m, n, k, ep);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<EPI, BN>, ma, mw, mo, m, n, k, ep);
     if (e != cudaSuccess) {
         record_cuda_error(e);
         return VDIT_ERR_LAUNCH;
@@ -408,7 +410,7 @@ extern "C" int vdit_linear(const void* a, int64_t lda, const void* w, int64_t ld
                            int64_t ldo, int64_t m, int32_t n, int32_t k, vdit_stream_t stream) {
     using namespace vdit::gemm;
     if (!a || !w || !out || m < 0 || n <= 0 || k <= 0) return VDIT_ERR_ARG;
-    if (n % BN || k % BK) return VDIT_ERR_UNSUPPORTED;
+    if (n % BN_FULL || k % BK) return VDIT_ERR_UNSUPPORTED;
     if (lda < k || ldw < k || ldo < n) return VDIT_ERR_ARG;
     if (!aligned16(a) || !aligned16(w) || !aligned16(out) || (bias && !aligned16(bias)) || lda % 8 || ldw % 8 ||
         ldo % 8)
@@ -416,10 +418,10 @@ extern "C" int vdit_linear(const void* a, int64_t lda, const void* w, int64_t ld
     if (m == 0) return VDIT_OK;
     if (m > (int64_t)INT32_MAX) return VDIT_ERR_UNSUPPORTED;
     CUtensorMap ma, mw, mo;
-    if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, BNH) || !make_map(&mo, out, m, n, ldo, 32, 64))
+    if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, BN_FULL / 2) || !make_map(&mo, out, m, n, ldo, 32, 64))
         return VDIT_ERR_DRIVER;
     EpiArgs ep{static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out), ldo};
-    return launch<EPI_BIAS>(ma, mw, mo, m, n, k, ep, static_cast<cudaStream_t>(stream));
+    return launch<EPI_BIAS, BN_FULL>(ma, mw, mo, m, n, k, ep, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int vdit_linear_qkv_rope3d(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias,
@@ -431,9 +433,11 @@ extern "C" int vdit_linear_qkv_rope3d(const void* a, int64_t lda, const void* w,
     if (!a || !w || !bias || !q_scale || !k_scale || !cos_t || !sin_t || !coords || !dst_rows || !out || m < 0 ||
         heads <= 0 || k <= 0 || res <= 0)
         return VDIT_ERR_ARG;
-    const int64_t n64 = 3LL * heads * head_dim;
-    if (head_dim != kQkvHd || n64 % BN || k % BK || n64 > INT32_MAX) return VDIT_ERR_UNSUPPORTED;
-    if ((int64_t)res * kQkvM * 2 * 4 > (int64_t)sizeof(Smem::ostage)) return VDIT_ERR_UNSUPPORTED;
+    if (head_dim != 128 && head_dim != 96) return VDIT_ERR_UNSUPPORTED;
+    const int bn = 2 * head_dim;                 // a pair tile: two whole heads of one section
+    const int64_t d = (int64_t)heads * head_dim, n64 = 3 * d;
+    if (d % bn || k % BK || n64 > INT32_MAX) return VDIT_ERR_UNSUPPORTED;
+    if ((int64_t)res * (head_dim / 6) * 2 * 4 > (int64_t)sizeof(Smem<BN_FULL>::ostage)) return VDIT_ERR_UNSUPPORTED;
     const int n = (int)n64;
     if (lda < k || ldw < k || ldo < n) return VDIT_ERR_ARG;
     if (!aligned16(a) || !aligned16(w) || !aligned16(out) || !aligned16(bias) || !aligned16(q_scale) ||
@@ -442,9 +446,10 @@ extern "C" int vdit_linear_qkv_rope3d(const void* a, int64_t lda, const void* w,
     if (m == 0) return VDIT_OK;
     if (m > (int64_t)INT32_MAX) return VDIT_ERR_UNSUPPORTED;
     CUtensorMap ma, mw, mo;
-    if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, BNH) || !make_map(&mo, out, m, n, ldo, 32, 64))
+    if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, bn / 2) || !make_map(&mo, out, m, n, ldo, 32, 64))
         return VDIT_ERR_DRIVER;
     EpiArgs ep{static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out), ldo, q_scale, k_scale,
-               cos_t, sin_t, reinterpret_cast<const int4*>(coords), dst_rows, heads * head_dim, res};
-    return launch<EPI_QKV>(ma, mw, mo, m, n, k, ep, static_cast<cudaStream_t>(stream));
+               cos_t, sin_t, reinterpret_cast<const int4*>(coords), dst_rows, (int)d, res};
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return head_dim == 128 ? launch<EPI_QKV, 256>(ma, mw, mo, m, n, k, ep, s) : launch<EPI_QKV, 192>(ma, mw, mo, m, n, k, ep, s);
 }

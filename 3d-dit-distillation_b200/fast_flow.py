@@ -101,8 +101,9 @@ class OptimizedLatDitRunner:
         self.overlap_branches = True
         self._neg_stream: Optional[torch.cuda.Stream] = None
         # the self-attention to_qkv GEMM runs QK-norm, RoPE3D and the window-order scatter
-        # in its epilogue (tcgen05 GEMM) where the head layout allows (head_dim 128, even heads)
-        self.fused_qkv = self.head_dim == 128 and (3 * self.dim) % 256 == 0
+        # in its epilogue (tcgen05 GEMM) where the head layout allows (head_dim 96 or 128,
+        # an even number of heads: a pair tile holds two whole heads of one section)
+        self.fused_qkv = self.head_dim in (96, 128) and self.num_heads % 2 == 0
         # CUDA-graph replay of the sampler (per voxel count, context length and schedule)
         self.cuda_graph = bool(cuda_graph)
         self._graphs: "OrderedDict[tuple, _SampleGraph]" = OrderedDict()

@@ -392,11 +392,12 @@ def test_linear_rejects_bad_shapes():
                   torch.zeros(100, 128, device=DEV, dtype=torch.bfloat16))
 
 
-@pytest.mark.parametrize("n,heads,res", [(3000, 12, 128), (16384, 12, 64), (300, 2, 64)])
-def test_linear_qkv_rope3d_matches_two_pass(n, heads, res):
+@pytest.mark.parametrize("n,heads,hd,res", [(3000, 12, 128, 128), (16384, 12, 128, 64), (300, 2, 128, 64),
+                                             (3000, 16, 96, 64), (5000, 2, 96, 128)])
+def test_linear_qkv_rope3d_matches_two_pass(n, heads, hd, res):
     """The fused epilogue against the two-pass path (GEMM, then the QK-norm / RoPE /
     gather kernel) and the fp32 oracle; rows land at bwd[r]."""
-    hd, K = 128, 1536
+    K = 1536
     vox = unique_cells(n, res, n + heads)
     _, _, hc = fk.lex_perm(torch.from_numpy(vox).to(DEV))
     g = torch.Generator(device=DEV).manual_seed(n + res)
@@ -411,7 +412,7 @@ def test_linear_qkv_rope3d_matches_two_pass(n, heads, res):
     bwd[fwd] = torch.arange(n, device=DEV)
     cos, sin = fk.precompute_rope_3d_table(res, 128.0, hd, device=DEV)
     fused = fk.linear_qkv_rope3d(a, w, b, qs, ks, cos, sin, hc, bwd, heads, hd)
-    two = fk.fused_qknorm_rope3d_gather(fk.linear(a, w, b), qs, ks, cos, sin, hc, fwd, heads, hd)
+    two = fk.fused_qknorm_rope3d_gather(torch.nn.functional.linear(a, w, b), qs, ks, cos, sin, hc, fwd, heads, hd)
     d = (fused.float() - two.float()).abs()
     # same bf16 GEMM output; only the order of the RMS sum differs (a rare 1-ulp bf16 flip)
     assert float((d > 0).float().mean()) < 1e-3 and float(d.max()) <= 0.0625
@@ -429,7 +430,7 @@ def test_linear_qkv_rope3d_rejects_odd_shapes():
     hc = torch.zeros(n, 4, device=DEV, dtype=torch.int32)
     bwd = torch.arange(n, device=DEV)
     cos, sin = fk.precompute_rope_3d_table(64, 128.0, 128, device=DEV)
-    for heads, hd in ((3, 128), (2, 96)):                          # 3*H*128 % 256 != 0; head_dim 96
+    for heads, hd in ((3, 128), (3, 96), (2, 64)):                 # odd head counts; head_dim 64
         D = heads * hd
         with pytest.raises(RuntimeError, match="unsupported"):
             fk.linear_qkv_rope3d(a, torch.zeros(3 * D, K, device=DEV, dtype=torch.bfloat16),
