@@ -325,6 +325,23 @@ def test_attention_scatter_and_large_logits():
     assert rel(out[rows], ref) < 1e-2
 
 
+def test_attention_late_dominant_keys():
+    """Keys in later tiles whose scores exceed every earlier score by hundreds (in log2
+    units): the running max jumps far past what the deferred rescale absorbs."""
+    heads, hd, n = 4, 128, 4096
+    g = torch.Generator(device=DEV).manual_seed(2)
+    qkv = torch.randn(n, 3 * heads * hd, device=DEV, generator=g)
+    D = heads * hd
+    qkv[:, :D] *= 6.0
+    for r in (1000, 2500, 4000):                              # keys in tiles 7, 19 and 31
+        qkv[r, D:2 * D] *= 40.0
+    qkv = qkv.to(torch.bfloat16)
+    out = fk.flash_varlen_qkvpacked_already_sorted(qkv, torch.tensor([0, n]), n, heads, hd)
+    ref = ref_attention(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], [0, n], [0, n], heads, hd)
+    assert bool(torch.isfinite(out.float()).all())
+    assert rel(out, ref) < 1e-2
+
+
 @pytest.mark.parametrize("n,heads,hd", [(1, 12, 128), (1000, 12, 128), (16384, 12, 128), (5000, 16, 96)])
 def test_attention_1q(n, heads, hd):
     g = torch.Generator(device=DEV).manual_seed(n)
