@@ -37,25 +37,34 @@ using namespace tc;
 
 constexpr int BM = 128;             // rows per CTA (256 per pair)
 constexpr int BN_FULL = 256;        // output columns per pair tile (192 for the head_dim-96 qkv)
-constexpr int BK = 64, STAGES = 6;
+constexpr int BK = 64;
 constexpr int EPI_WARPS = 4;
 constexpr int THREADS = (2 + EPI_WARPS) * 32;
 constexpr int kErr = 0x474D;   // "GM": a bounded wait of the GEMM kernel ran out
-
-template <int BN>
-struct __align__(1024) Smem {
-    uint8_t a[STAGES][BM * 128];
-    uint8_t b[STAGES][BN / 2 * 128];    // this CTA's half of the weight tile
-    uint8_t ostage[EPI_WARPS][2][32 * 128];   // per epilogue warp: two 32-row x 64-column bf16 boxes
-    uint64_t full[STAGES], empty[STAGES], acc_full[2], acc_empty[2];
-    uint32_t tmem_slot;
-    int abort_flag;
-};
 
 // epilogue kinds
 constexpr int EPI_BIAS = 0;   // out = bf16(acc + bias)
 constexpr int EPI_QKV = 1;    // self-attention qkv: QK-RMSNorm + 3D RoPE, rows scattered to window order;
                               // a pair tile holds two whole heads (BN = 2 * head_dim, 256 or 192)
+constexpr int kQkvTableBytes = 24576;   // EPI_QKV: RoPE cos + sin tables staged in shared memory
+
+// EPI_BIAS: a 6-stage ring and, per epilogue warp, two 32-row x 64-column bf16 boxes stored
+// by TMA.  EPI_QKV: a 4-stage ring, the RoPE tables and, per epilogue warp, two buffers of
+// 32 head rows (one per head of the tile), padded to spread the lanes' stores over the
+// banks; each row leaves with its own bulk copy to its scattered output row.
+template <int EPI, int BN>
+struct __align__(1024) Smem {
+    static constexpr int NST = EPI == EPI_QKV ? 4 : 6;
+    static constexpr int ROWPAD = BN + 16;                 // a head row: BN / 2 bf16 = BN bytes
+    static constexpr int XBYTES =
+        EPI == EPI_QKV ? kQkvTableBytes + EPI_WARPS * 2 * 32 * ROWPAD : EPI_WARPS * 2 * 32 * 128;
+    uint8_t a[NST][BM * 128];
+    uint8_t b[NST][BN / 2 * 128];    // this CTA's half of the weight tile
+    uint8_t x[XBYTES];
+    uint64_t full[NST], empty[NST], acc_full[2], acc_empty[2];
+    uint32_t tmem_slot;
+    int abort_flag;
+};
 
 struct EpiArgs {
     const __nv_bfloat16* bias;   // [N] or null
@@ -99,7 +108,9 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
     constexpr uint32_t kStageBytes = (BM + BNH) * 128;   // per CTA and k-step
     constexpr int kQkvHd = BN / 2;                   // EPI_QKV: head_dim (two heads per tile)
     constexpr int kQkvM = kQkvHd / 6;                // RoPE frequencies per axis (x, y, z)
-    Smem<BN>& sm = *reinterpret_cast<Smem<BN>*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    using SM = Smem<EPI, BN>;
+    constexpr int STAGES = SM::NST;
+    SM& sm = *reinterpret_cast<SM*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
@@ -125,7 +136,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmO)) : "memory");
     }
     if (EPI == EPI_QKV) {   // RoPE tables into the staging area (this epilogue stores from registers)
-        float* tab = reinterpret_cast<float*>(&sm.ostage[0][0][0]);
+        float* tab = reinterpret_cast<float*>(sm.x);
         const int nt = ep.res * kQkvM;
         for (int i = threadIdx.x; i < nt; i += THREADS) {
             tab[i] = __ldg(ep.cos_t + i);
@@ -232,7 +243,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
                             for (int j = 0; j < 8; ++j) v[q * 8 + j] += bv[j];
                         }
                     }
-                    uint8_t* box = sm.ostage[ew][nstore & 1];
+                    uint8_t* box = sm.x + (ew * 2 + (nstore & 1)) * 32 * 128;
                     if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
                     __syncwarp();
 #pragma unroll
@@ -261,7 +272,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
                     tr[1] = min(max(c.z, 0), ep.res - 1) * kQkvM;
                     tr[2] = min(max(c.w, 0), ep.res - 1) * kQkvM;
                 }
-                const float* cs_s = reinterpret_cast<const float*>(&sm.ostage[0][0][0]);
+                const float* cs_s = reinterpret_cast<const float*>(sm.x);
                 const float* sn_s = cs_s + ep.res * kQkvM;
 #pragma unroll 1
                 for (int hh = 0; hh < BN / kQkvHd; ++hh) {
@@ -305,18 +316,27 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
                             }
                         }
                     }
+                    // the row into this head's buffer (free once the previous tile's copy of it has
+                    // been read), then one bulk copy of its kQkvHd * 2 bytes to the scattered row
+                    uint8_t* rb = sm.x + kQkvTableBytes + ((ew * 2 + hh) * 32 + lane) * SM::ROWPAD;
+                    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+#pragma unroll
+                    for (int q = 0; q < kQkvHd / 8; ++q) *reinterpret_cast<uint4*>(rb + q * 16) = pack8(x + q * 8);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     if (live) {
                         __nv_bfloat16* dst = ep.out + orow * ep.ldo + col;
-#pragma unroll
-                        for (int q = 0; q < kQkvHd / 8; ++q) *reinterpret_cast<uint4*>(dst + q * 8) = pack8(x + q * 8);
+                        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                                     ::"l"(reinterpret_cast<uint64_t>(dst)), "r"(smem_u32(rb)), "r"(kQkvHd * 2)
+                                     : "memory");
                     }
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&sm.acc_empty[buf]), 0));
         }
-        if (EPI == EPI_BIAS && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        if (EPI == EPI_QKV || lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
 
     tc_fence_before();
@@ -354,7 +374,7 @@ int num_sms() {
 template <int EPI, int BN>
 int launch(const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo, int64_t m, int n, int k,
            const EpiArgs& ep, cudaStream_t s) {
-    const size_t smem = sizeof(Smem<BN>) + 1024;
+    const size_t smem = sizeof(Smem<EPI, BN>) + 1024;
     static int max_pairs = 0;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -437,7 +457,7 @@ extern "C" int vdit_linear_qkv_rope3d(const void* a, int64_t lda, const void* w,
     const int bn = 2 * head_dim;                 // a pair tile: two whole heads of one section
     const int64_t d = (int64_t)heads * head_dim, n64 = 3 * d;
     if (d % bn || k % BK || n64 > INT32_MAX) return VDIT_ERR_UNSUPPORTED;
-    if ((int64_t)res * (head_dim / 6) * 2 * 4 > (int64_t)sizeof(Smem<BN_FULL>::ostage)) return VDIT_ERR_UNSUPPORTED;
+    if ((int64_t)res * (head_dim / 6) * 2 * 4 > kQkvTableBytes) return VDIT_ERR_UNSUPPORTED;
     const int n = (int)n64;
     if (lda < k || ldw < k || ldo < n) return VDIT_ERR_ARG;
     if (!aligned16(a) || !aligned16(w) || !aligned16(out) || !aligned16(bias) || !aligned16(q_scale) ||

@@ -232,7 +232,7 @@ int vdit_linear(const void* a, int64_t lda, const void* w, int64_t ldw, const vo
  * vdit_linear followed by vdit_qknorm_rope3d_gather with fwd = the inverse of
  * dst_rows (lib/fast_flow.py:1450-1464, lib/fast_kernels.py:1476-1535).
  * head_dim 128 or 96 with an even number of heads (a CTA pair's tile holds two whole
- * heads); cos_t/sin_t [res, head_dim/6] fp32 (res <= 195 at 128, 256 at 96);
+ * heads); cos_t/sin_t [res, head_dim/6] fp32 (res <= 146 at 128, 192 at 96);
  * q_scale/k_scale [heads*head_dim] fp32; coords int32 [m, 4]; dst_rows int64 [m], a
  * permutation of 0..m-1. */
 int vdit_linear_qkv_rope3d(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias,
