@@ -301,8 +301,8 @@ __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_
                  : "memory");
 }
 
-// Accumulates one group of 4 rows over its union taps; the next tap's slots
-// and index are fetched while the current one computes.
+// Accumulates one group of 4 rows over its union taps, two taps per iteration
+// (both taps' loads issued before their FMAs).
 template <bool GLOBAL>
 __device__ __forceinline__ void accumulate_group(const Group* grp, const char* feat, const char* wb, int lane,
                                                  const __nv_bfloat16* __restrict__ hcol, int c,
@@ -310,11 +310,9 @@ __device__ __forceinline__ void accumulate_group(const Group* grp, const char* f
     const int nt = grp->ntaps;
     const char* fl = feat + lane * 8;
     const char* wl = wb + lane * 16;
-    int4 sl = grp->slots[0];
-    int d = grp->taps[0];
-    for (int i = 0; i < nt; ++i) {
+    auto load_tap = [&](int i, uint2 (&v)[kGroupRows], float4& wv) {
+        const int4 sl = grp->slots[i];
         const int s[kGroupRows] = {sl.x, sl.y, sl.z, sl.w};
-        uint2 v[kGroupRows];
 #pragma unroll
         for (int q = 0; q < kGroupRows; ++q) {
             if (GLOBAL) {
@@ -325,17 +323,30 @@ __device__ __forceinline__ void accumulate_group(const Group* grp, const char* f
                 v[q] = *reinterpret_cast<const uint2*>(fl + s[q]);
             }
         }
-        const float4 wv = *reinterpret_cast<const float4*>(wl + d * kWRowBytes);
-        // slots[27] / taps[27] past the last tap are in bounds of the record or the next
-        // one and are never used
-        sl = grp->slots[i + 1];
-        d = grp->taps[i + 1];
+        wv = *reinterpret_cast<const float4*>(wl + grp->taps[i] * kWRowBytes);
+    };
+    auto fma_tap = [&](const uint2 (&v)[kGroupRows], const float4& wv) {
         const float2 wa = make_float2(wv.x, wv.y), wg = make_float2(wv.z, wv.w);
 #pragma unroll
         for (int q = 0; q < kGroupRows; ++q) {
             acc_a[q] = tc::ffma2v(unpack_bf2(v[q].x), wa, acc_a[q]);
             acc_g[q] = tc::ffma2v(unpack_bf2(v[q].y), wg, acc_g[q]);
         }
+    };
+    int i = 0;
+    for (; i + 1 < nt; i += 2) {
+        uint2 v0[kGroupRows], v1[kGroupRows];
+        float4 w0, w1;
+        load_tap(i, v0, w0);
+        load_tap(i + 1, v1, w1);
+        fma_tap(v0, w0);
+        fma_tap(v1, w1);
+    }
+    if (i < nt) {
+        uint2 v0[kGroupRows];
+        float4 w0;
+        load_tap(i, v0, w0);
+        fma_tap(v0, w0);
     }
 }
 
