@@ -85,8 +85,8 @@ __global__ void __launch_bounds__(256) modulate_kernel(const __nv_bfloat16* __re
 // x <- bf16(x + h * g); optional mod_out = LN(x) * s1 + sh
 __global__ void __launch_bounds__(256) gate_add_modulate_kernel(
     __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ h, int64_t h_stride, int64_t m, int d,
-    const float* __restrict__ g, const float* __restrict__ s1, const float* __restrict__ sh,
-    __nv_bfloat16* __restrict__ mod_out) {
+    const float* __restrict__ g, const __nv_bfloat16* __restrict__ c2, const float* __restrict__ g2,
+    const float* __restrict__ s1, const float* __restrict__ sh, __nv_bfloat16* __restrict__ mod_out) {
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int64_t row = blockIdx.x * (int64_t)kRowWarps + warp;
     if (row >= m) return;
@@ -104,12 +104,25 @@ __global__ void __launch_bounds__(256) gate_add_modulate_kernel(
         float4 g0 = __ldg(reinterpret_cast<const float4*>(g + vi * 8));
         float4 g1 = __ldg(reinterpret_cast<const float4*>(g + vi * 8 + 4));
         float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        float cv[8], gv2[8];
+        if (c2) {
+            load8_nc(c2 + vi * 8, cv);
+            const float4 a0 = __ldg(reinterpret_cast<const float4*>(g2 + vi * 8));
+            const float4 a1 = __ldg(reinterpret_cast<const float4*>(g2 + vi * 8 + 4));
+            const float t8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) gv2[j] = t8[j];
+        }
         uint4 packed;
         __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&packed);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             p2[j] = __floats2bfloat162_rn(xv[2 * j] + hv[2 * j] * gg[2 * j], xv[2 * j + 1] + hv[2 * j + 1] * gg[2 * j + 1]);
             float2 t = __bfloat1622float2(p2[j]);
+            if (c2) {       // second residual, rounded like a second gate-add pass
+                p2[j] = __floats2bfloat162_rn(t.x + cv[2 * j] * gv2[2 * j], t.y + cv[2 * j + 1] * gv2[2 * j + 1]);
+                t = __bfloat1622float2(p2[j]);
+            }
             r.v[i][2 * j] = t.x;
             r.v[i][2 * j + 1] = t.y;
         }
@@ -129,6 +142,7 @@ __global__ void __launch_bounds__(256) gate_add_modulate_kernel(
 // Arithmetic is identical to the one-row-per-warp kernels.  Waits on the bulk
 // copies are bounded; a timeout sets the row kernels' error word.
 constexpr int kGaMaxWarps = 16;
+constexpr int kGaVecBytes = 20;          // shared fp32 vectors per column: g, s1, sh, g2, c2
 constexpr int kErrRowTimeout = 0x524f;   // "RO": a bounded wait of a row kernel ran out
 
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
@@ -139,8 +153,8 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
 
 __global__ void __launch_bounds__(kGaMaxWarps * 32, 1) gate_add_modulate_staged_kernel(
     __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ h, int64_t h_stride, int64_t m, int d,
-    const float* __restrict__ g, const float* __restrict__ s1, const float* __restrict__ sh,
-    __nv_bfloat16* __restrict__ mod_out) {
+    const float* __restrict__ g, const __nv_bfloat16* __restrict__ c2, const float* __restrict__ g2,
+    const float* __restrict__ s1, const float* __restrict__ sh, __nv_bfloat16* __restrict__ mod_out) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int abort_flag;
     const int nwarps = blockDim.x >> 5;
@@ -150,15 +164,22 @@ __global__ void __launch_bounds__(kGaMaxWarps * 32, 1) gate_add_modulate_staged_
     float* pg = reinterpret_cast<float*>(smem);
     float* ps1 = pg + d;
     float* psh = ps1 + d;
+    float* pg2 = psh + d;            // second residual: its gate and its (broadcast) row in fp32
+    float* pc2 = pg2 + d;
     const uint32_t row_bytes = 2u * (uint32_t)d;
-    uint8_t* wbuf = smem + (size_t)12 * d + (size_t)warp * 4 * row_bytes;   // [stage][x | h]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)12 * d + (size_t)nwarps * 4 * row_bytes) + warp * 2;
+    uint8_t* wbuf = smem + (size_t)kGaVecBytes * d + (size_t)warp * 4 * row_bytes;   // [stage][x | h]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kGaVecBytes * d + (size_t)nwarps * 4 * row_bytes) +
+                     warp * 2;
     const uint32_t bar_u[2] = {tc::smem_u32(bars), tc::smem_u32(bars + 1)};
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
         if (add) pg[i] = g[i];
         if (mod) {
             ps1[i] = s1[i];
             psh[i] = sh[i];
+        }
+        if (c2) {
+            pg2[i] = g2[i];
+            pc2[i] = bf2f(c2[i]);
         }
     }
     if (threadIdx.x == 0) abort_flag = 0;
@@ -210,7 +231,12 @@ __global__ void __launch_bounds__(kGaMaxWarps * 32, 1) gate_add_modulate_staged_
             for (int j = 0; j < 4; ++j) {
                 p2[j] = __floats2bfloat162_rn(xv[2 * j] + hv[2 * j] * gg[2 * j],
                                               xv[2 * j + 1] + hv[2 * j + 1] * gg[2 * j + 1]);
-                const float2 t = __bfloat1622float2(p2[j]);
+                float2 t = __bfloat1622float2(p2[j]);
+                if (c2) {   // second residual, rounded like a second gate-add pass
+                    const int e = vi * 8 + 2 * j;
+                    p2[j] = __floats2bfloat162_rn(t.x + pc2[e] * pg2[e], t.y + pc2[e + 1] * pg2[e + 1]);
+                    t = __bfloat1622float2(p2[j]);
+                }
                 r.v[i][2 * j] = t.x;
                 r.v[i][2 * j + 1] = t.y;
             }
@@ -556,7 +582,8 @@ using namespace vdit;
 static bool row_width_ok(int32_t d) { return d > 0 && d % 8 == 0 && d <= 256 * kMaxVec; }
 
 int launch_gate_add_staged(__nv_bfloat16* x, const __nv_bfloat16* h, int64_t h_stride, int64_t m, int d,
-                           const float* g, const float* s1, const float* sh, __nv_bfloat16* mod_out, cudaStream_t s) {
+                           const float* g, const __nv_bfloat16* c2, const float* g2, const float* s1, const float* sh,
+                           __nv_bfloat16* mod_out, cudaStream_t s) {
     static int sms[64] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -566,7 +593,7 @@ int launch_gate_add_staged(__nv_bfloat16* x, const __nv_bfloat16* h, int64_t h_s
     }
     constexpr size_t kMaxSmem = 227 * 1024 - 256;
     const size_t per_warp = (size_t)8 * d + 16;
-    const int nwarps = (int)std::min<size_t>(kGaMaxWarps, (kMaxSmem - (size_t)12 * d) / per_warp);
+    const int nwarps = (int)std::min<size_t>(kGaMaxWarps, (kMaxSmem - (size_t)kGaVecBytes * d) / per_warp);
     if (sms[dev] == 0) {
         int n = 0;
         e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
@@ -579,9 +606,9 @@ int launch_gate_add_staged(__nv_bfloat16* x, const __nv_bfloat16* h, int64_t h_s
         }
         sms[dev] = n;
     }
-    const size_t smem = (size_t)12 * d + (size_t)nwarps * per_warp;
+    const size_t smem = (size_t)kGaVecBytes * d + (size_t)nwarps * per_warp;
     const unsigned grid = (unsigned)std::min<int64_t>((m + nwarps - 1) / nwarps, sms[dev]);
-    gate_add_modulate_staged_kernel<<<grid, nwarps * 32, smem, s>>>(x, h, h_stride, m, d, g, s1, sh, mod_out);
+    gate_add_modulate_staged_kernel<<<grid, nwarps * 32, smem, s>>>(x, h, h_stride, m, d, g, c2, g2, s1, sh, mod_out);
     count_launches(1);
     return check_launch();
 }
@@ -604,7 +631,7 @@ extern "C" int vdit_modulate(const void* x, int64_t m, int32_t d, const float* s
     if (m == 0) return VDIT_OK;
     if (m >= 4096)       // persistent CTAs with bulk-copied rows (the staged kernel without its gate-add)
         return launch_gate_add_staged(const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(x)), nullptr, 0, m,
-                                      d, nullptr, s1, sh, static_cast<__nv_bfloat16*>(out),
+                                      d, nullptr, nullptr, nullptr, s1, sh, static_cast<__nv_bfloat16*>(out),
                                       static_cast<cudaStream_t>(stream));
     modulate_kernel<<<blocks_for(m, kRowWarps), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16*>(x), m, d, s1, sh, static_cast<__nv_bfloat16*>(out));
@@ -612,23 +639,38 @@ extern "C" int vdit_modulate(const void* x, int64_t m, int32_t d, const float* s
     return check_launch();
 }
 
-extern "C" int vdit_gate_add_modulate(void* x, const void* h, int64_t h_stride, int64_t m, int32_t d, const float* g,
-                                      const float* s1, const float* sh, void* mod_out, vdit_stream_t stream) {
+static int gate_add_impl(void* x, const void* h, int64_t h_stride, int64_t m, int32_t d, const float* g,
+                         const void* c2, const float* g2, const float* s1, const float* sh, void* mod_out,
+                         vdit_stream_t stream) {
     if (m < 0 || !row_width_ok(d) || !x || !h || !g || h_stride < 0) return VDIT_ERR_ARG;
     if (mod_out && (!s1 || !sh)) return VDIT_ERR_ARG;
+    if ((c2 == nullptr) != (g2 == nullptr)) return VDIT_ERR_ARG;
     if (!aligned16(x) || !aligned16(h) || !aligned16(g) || (h_stride % 8) || (mod_out && !aligned16(mod_out)) ||
-        (s1 && !aligned16(s1)) || (sh && !aligned16(sh)))
+        (s1 && !aligned16(s1)) || (sh && !aligned16(sh)) || (c2 && !aligned16(c2)) || (g2 && !aligned16(g2)))
         return VDIT_ERR_ALIGN;
     if (m == 0) return VDIT_OK;
+    auto* xb = static_cast<__nv_bfloat16*>(x);
+    auto* hb = static_cast<const __nv_bfloat16*>(h);
+    auto* cb = static_cast<const __nv_bfloat16*>(c2);
+    auto* ob = static_cast<__nv_bfloat16*>(mod_out);
     if (m >= 4096)       // enough rows for persistent CTAs to pay off
-        return launch_gate_add_staged(static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(h), h_stride,
-                                      m, d, g, s1, sh, static_cast<__nv_bfloat16*>(mod_out),
-                                      static_cast<cudaStream_t>(stream));
+        return launch_gate_add_staged(xb, hb, h_stride, m, d, g, cb, g2, s1, sh, ob, static_cast<cudaStream_t>(stream));
     gate_add_modulate_kernel<<<blocks_for(m, kRowWarps), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(h), h_stride, m, d, g, s1, sh,
-        static_cast<__nv_bfloat16*>(mod_out));
+        xb, hb, h_stride, m, d, g, cb, g2, s1, sh, ob);
     count_launches(1);
     return check_launch();
+}
+
+extern "C" int vdit_gate_add_modulate(void* x, const void* h, int64_t h_stride, int64_t m, int32_t d, const float* g,
+                                      const float* s1, const float* sh, void* mod_out, vdit_stream_t stream) {
+    return gate_add_impl(x, h, h_stride, m, d, g, nullptr, nullptr, s1, sh, mod_out, stream);
+}
+
+extern "C" int vdit_gate_add2_modulate(void* x, const void* h, int64_t h_stride, int64_t m, int32_t d, const float* g,
+                                       const void* c2, const float* g2, const float* s1, const float* sh,
+                                       void* mod_out, vdit_stream_t stream) {
+    if (!c2 || !g2) return VDIT_ERR_ARG;
+    return gate_add_impl(x, h, h_stride, m, d, g, c2, g2, s1, sh, mod_out, stream);
 }
 
 extern "C" int vdit_out_modulate_unpatchify(const void* x, int64_t m, int32_t d, const float* s1, const float* sh,

@@ -460,8 +460,8 @@ class OptimizedLatDitRunner:
                         C2 = CG2[bb - cd]
                         xc = mod_lin(C2[0], C2[1], "cr1_w", "cr1_b", self.blocks[bb])
                         consts.append((xc, on_side_event()))
-            if b >= start:
-                h = self._self_attention(b, h_mod, geom)
+            h = self._self_attention(b, h_mod, geom) if b >= start else None
+            if h is not None and b < cd:
                 h_mod = fk.fast_gate_add_and_modulate(x, h, G[b, 2], G[b, 3], G[b, 4])
             if b < cd:
                 kv_x = F.linear(h_mod, w["kvx_w"], w["kvx_b"])                     # [N, 2D]
@@ -485,7 +485,12 @@ class OptimizedLatDitRunner:
                 if two:
                     main.wait_event(ready)
                     x_const.record_stream(main)
-                h_mod = fk.fast_gate_add_and_modulate(x, x_const, G[b, 5], G[b, 6], G[b, 7], broadcast_h=True)
+                if h is not None:
+                    # the self-attention and the constant cross-attention gate-adds in one pass
+                    # (the modulation between them feeds nothing in this branch)
+                    h_mod = fk.fast_gate_add2_and_modulate(x, h, G[b, 2], x_const, G[b, 5], G[b, 6], G[b, 7])
+                else:
+                    h_mod = fk.fast_gate_add_and_modulate(x, x_const, G[b, 5], G[b, 6], G[b, 7], broadcast_h=True)
             hf = self._ffn(b, h_mod, geom)
             if b + 1 < self.depth:
                 h_mod = fk.fast_gate_add_and_modulate(x, hf, G[b, 8], G[b + 1, 0], G[b + 1, 1])

@@ -171,6 +171,25 @@ def fast_gate_add_and_modulate(x: torch.Tensor, h: torch.Tensor, gate: torch.Ten
     return mod
 
 
+def fast_gate_add2_and_modulate(x: torch.Tensor, h: torch.Tensor, gate: torch.Tensor, c_row: torch.Tensor,
+                                gate2: torch.Tensor, scale1: Optional[torch.Tensor], shift: Optional[torch.Tensor],
+                                out: Optional[torch.Tensor] = None):
+    """Two gate-adds in one pass: x += h * gate, then x += c_row * gate2 (one [D] row for
+    every row), each rounded to bf16 as its own pass would; returns LN(x) * scale1 + shift
+    (or None when scale1 is None)."""
+    m, d = x.shape
+    if c_row.dtype != BF16 or c_row.numel() != d or gate2.numel() != d:
+        raise ValueError(f"fast_gate_add2_and_modulate: c_row must be a bf16 row of {d}, gate2 of {d}")
+    mod = None
+    if scale1 is not None:
+        mod = torch.empty_like(x) if out is None else out
+    c = c_row.reshape(-1).contiguous()
+    g2 = _f32(gate2)
+    check(lib().vdit_gate_add2_modulate(ptr(x), ptr(h), h.stride(0), m, d, ptr(gate), ptr(c), ptr(g2), ptr(scale1),
+                                        ptr(shift), ptr(mod), _s(x)), "gate_add2_modulate")
+    return mod
+
+
 def fast_gate_add(x: torch.Tensor, h: torch.Tensor, gate: torch.Tensor, broadcast_h: bool = False) -> torch.Tensor:
     fast_gate_add_and_modulate(x, h, gate, None, None, broadcast_h=broadcast_h)
     return x

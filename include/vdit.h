@@ -101,6 +101,15 @@ int vdit_gate_add_modulate(void* x, const void* h, int64_t h_row_stride, int64_t
                            const float* gate, const float* scale1, const float* shift,
                            void* mod_out, vdit_stream_t stream);
 
+/* Two gated residuals in one pass: x <- bf16(bf16(x + h * gate) + c2 * gate2), with c2
+ * bf16 [d] one row broadcast to all rows, then (mod_out != NULL) the LayerNorm
+ * modulation.  The 1-token branch's self-attention gate-add followed by its constant
+ * cross-attention gate-add (BK/models/generators/lat_dit.py:345,473; lib/fast_flow.py:
+ * 2295-2309), rounded as the two separate passes round. */
+int vdit_gate_add2_modulate(void* x, const void* h, int64_t h_row_stride, int64_t m, int32_t d,
+                            const float* gate, const void* c2, const float* gate2, const float* scale1,
+                            const float* shift, void* mod_out, vdit_stream_t stream);
+
 /* out[m,16] fp32 = bf16(LN(x) * scale1 + shift) @ w[16,d]^T.  Replaces
  * _fused_out_modulate_unpatchify_kernel (lib/fast_kernels.py:613-648, 888-940). */
 int vdit_out_modulate_unpatchify(const void* x, int64_t m, int32_t d, const float* scale1,

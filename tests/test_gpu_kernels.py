@@ -112,6 +112,23 @@ def test_modulate_and_gate_add(m, d):
     assert rel(x3, x.float() + h[0].float() * gt) < 5e-3
 
 
+@pytest.mark.parametrize("m,d", [(700, 1536), (5000, 1536), (4096, 768)])
+def test_gate_add2_matches_two_passes(m, d):
+    """Two gated residuals in one pass (the second a broadcast row) against two gate-add
+    passes: the same bits, then the same modulation."""
+    g = torch.Generator(device=DEV).manual_seed(m + 3)
+    x = torch.randn(m, d, device=DEV, generator=g).to(torch.bfloat16)
+    h = torch.randn(m, d, device=DEV, generator=g).to(torch.bfloat16)
+    c = torch.randn(d, device=DEV, generator=g).to(torch.bfloat16)
+    g1, g2, s1, sh = [torch.randn(d, device=DEV, generator=g) * 0.3 + o for o in (0.0, 0.0, 1.0, 0.0)]
+    xa = x.clone()
+    ma = fk.fast_gate_add2_and_modulate(xa, h, g1, c, g2, s1, sh)
+    xb = x.clone()
+    fk.fast_gate_add_and_modulate(xb, h, g1, None, None)
+    mb = fk.fast_gate_add_and_modulate(xb, c, g2, s1, sh, broadcast_h=True)
+    assert torch.equal(xa, xb) and torch.equal(ma, mb)
+
+
 @pytest.mark.parametrize("m,d,stride_h", [(4096, 1536, False), (9001, 1536, True), (5000, 768, False)])
 def test_gate_add_staged_matches_rowwise(m, d, stride_h):
     """m >= 4096 rows take the persistent staged kernel; chunks below that the
