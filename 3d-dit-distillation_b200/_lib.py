@@ -48,6 +48,9 @@ SIGNATURES = {
     "vdit_attention": (ctypes.c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _vp, _vp, _vp, _c_i32,
                                       _c_i32, _c_i32, _c_f32, _vp]),
     "vdit_attention_1q_workspace_bytes": (_c_sz, [_c_i32, _c_i32, _c_i64]),
+    "vdit_attention_1q_wide_workspace_bytes": (_c_sz, [_c_i32, _c_i32, _c_i64]),
+    "vdit_attention_1q_wide": (ctypes.c_int, [_vp, _vp, _c_i64, _c_i64, _vp, _vp, _c_i64, _vp, _c_i32, _c_i32, _c_f32,
+                                              _vp, _vp, _c_sz, _vp]),
     "vdit_attention_1q": (ctypes.c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_f32, _vp, _vp, _c_sz,
                                          _vp]),
     "vdit_attention_1q_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_f32, _vp, _vp]),

@@ -1,0 +1,261 @@
+// The context->x attention of the exact 1-token branch without materialising the
+// voxels' keys and values.  In the reference the single context query of each head
+// attends over K = h Wk^T + bk and V = h Wv^T + bv, the rows of the cross linear of
+// the modulated voxel stream h [n, D] (lib/fast_flow.py:1769-1777).  Since
+//   q_h . K[r, h] = h[r] . (Wk_h^T q_h) + q_h . bk_h   (the second term is the same
+//   for every key and cancels in the softmax), and
+//   sum_r p[r, h] V[r, h] = Wv_h (sum_r p[r, h] h[r]) + bv_h   (sum_r p = 1),
+// the attention runs on h directly: fold each query through Wk (qf [H, D] fp32),
+// stream h once computing the H scores of every row in fp32 with an online softmax and
+// the probability-weighted row sums u_h = sum_r p h[r] (split over row ranges), then
+// combine the splits and apply Wv and bv.  HBM traffic: one read of h (n x D bf16)
+// instead of writing and reading the [n, 2D] K/V.
+#include <math.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace vdit {
+namespace {
+
+constexpr int kRows = 8;               // rows per batch of the streaming pass
+constexpr int kHg = 4;                 // heads per block (kRows * kHg = 32 partial scores per thread)
+constexpr int kMaxHeads = 16;
+constexpr int kRowsPerRange = 128;
+constexpr int kFoldThreads = 256;
+constexpr int kCombThreads = 256;
+
+// qf[h, d] = scale_log2 * sum_j q[h*hd + j] * wk[(h*hd + j), d]
+__global__ void __launch_bounds__(kFoldThreads) wide1q_fold_kernel(const __nv_bfloat16* __restrict__ q,
+                                                                   const __nv_bfloat16* __restrict__ wk,
+                                                                   int64_t ldw, int d, int hd, float scale_log2,
+                                                                   float* __restrict__ qf) {
+    __shared__ float qs[256];
+    const int h = blockIdx.y;
+    const int col = blockIdx.x * kFoldThreads + threadIdx.x;
+    for (int j = threadIdx.x; j < hd; j += kFoldThreads) qs[j] = bf2f(q[(int64_t)h * hd + j]);
+    __syncthreads();
+    if (col >= d) return;
+    const __nv_bfloat16* w = wk + (int64_t)h * hd * ldw + col;
+    float acc = 0.f;
+    for (int j = 0; j < hd; ++j) acc = fmaf(qs[j], bf2f(w[(int64_t)j * ldw]), acc);
+    qf[(int64_t)h * d + col] = acc * scale_log2;
+}
+
+// A block handles one range of rows for one group of kHg heads (the groups of a range
+// are adjacent blocks, so the range's rows are read from HBM once and from L2 after).
+// Thread t owns columns [4t, 4t + 4) of its heads' folded queries and weighted row sums.
+// Per batch of kRows rows: kRows x kHg partial scores per thread, reduced across the warp
+// by recursive halving (lane L ends with value L: row L / kHg, head L % kHg), then
+// across warps through shared memory; one thread per head updates the running max / sum
+// and turns the scores into probabilities; every thread rescales and accumulates u.
+__global__ void wide1q_partial_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t n, int d, int heads,
+                                      const float* __restrict__ qf, int64_t per, float* __restrict__ ws) {
+    constexpr int V = kRows * kHg;                   // 32: one reduced value per lane
+    __shared__ float red[16][V];                     // up to 512 threads
+    __shared__ float sc[V];                          // scores, then probabilities
+    __shared__ float alpha[kHg], mstate[kHg], lstate[kHg];
+    const int ngroups = (heads + kHg - 1) / kHg;
+    const int rr = blockIdx.x / ngroups, hg = blockIdx.x % ngroups;
+    const int nwarps = blockDim.x >> 5;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int col = 4 * t;
+    const int64_t r0 = (int64_t)rr * per, r1 = min(n, r0 + per);
+
+    float q4[kHg][4], u[kHg][4];
+#pragma unroll
+    for (int hl = 0; hl < kHg; ++hl) {
+        const int h = hg * kHg + hl;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            q4[hl][k] = h < heads ? qf[(int64_t)h * d + col + k] : 0.f;
+            u[hl][k] = 0.f;
+        }
+    }
+    if (t < kHg) {
+        mstate[t] = -INFINITY;
+        lstate[t] = 0.f;
+    }
+
+    for (int64_t b = r0; b < r1; b += kRows) {
+        float hv[kRows][4];
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+            if (b + r < r1) {
+                const uint2 raw = __ldg(reinterpret_cast<const uint2*>(x + (b + r) * ldx + col));
+                const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+                const float2 a = __bfloat1622float2(p2[0]), c = __bfloat1622float2(p2[1]);
+                hv[r][0] = a.x;
+                hv[r][1] = a.y;
+                hv[r][2] = c.x;
+                hv[r][3] = c.y;
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) hv[r][k] = 0.f;
+            }
+        }
+        float val[V];
+#pragma unroll
+        for (int r = 0; r < kRows; ++r)
+#pragma unroll
+            for (int hl = 0; hl < kHg; ++hl)
+                val[r * kHg + hl] =
+                    hv[r][0] * q4[hl][0] + hv[r][1] * q4[hl][1] + hv[r][2] * q4[hl][2] + hv[r][3] * q4[hl][3];
+        // recursive halving across the warp: after step s a lane keeps the half picked by bit 4-s
+#pragma unroll
+        for (int s = 0; s < 5; ++s) {
+            const int o = 16 >> s;
+            const int half = V >> (s + 1);
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < half; ++i) {
+                const float send = up ? val[i] : val[i + half];
+                const float recv = __shfl_xor_sync(0xffffffffu, send, o);
+                val[i] = (up ? val[i + half] : val[i]) + recv;
+            }
+        }
+        red[warp][lane] = val[0];
+        __syncthreads();
+        if (t < V) {
+            float s = 0.f;
+            for (int w = 0; w < nwarps; ++w) s += red[w][t];
+            sc[t] = (b + t / kHg < r1) ? s : -INFINITY;
+        }
+        __syncthreads();
+        if (t < kHg) {          // online softmax of head t of the group over this batch
+            const float m_old = mstate[t];
+            float mb = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < kRows; ++r) mb = fmaxf(mb, sc[r * kHg + t]);
+            const float m_new = fmaxf(m_old, mb);
+            const float a = m_old == -INFINITY ? 0.f : exp2f(m_old - m_new);
+            float l = lstate[t] * a;
+#pragma unroll
+            for (int r = 0; r < kRows; ++r) {
+                const float p = exp2f(sc[r * kHg + t] - m_new);
+                sc[r * kHg + t] = p;
+                l += p;
+            }
+            mstate[t] = m_new;
+            lstate[t] = l;
+            alpha[t] = a;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int hl = 0; hl < kHg; ++hl) {
+            const float a = alpha[hl];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                float acc = u[hl][k] * a;
+#pragma unroll
+                for (int r = 0; r < kRows; ++r) acc = fmaf(sc[r * kHg + hl], hv[r][k], acc);
+                u[hl][k] = acc;
+            }
+        }
+        __syncthreads();        // sc and alpha are rewritten by the next batch
+    }
+    // partial state of this row range: per head [m, l, u[d]]
+#pragma unroll
+    for (int hl = 0; hl < kHg; ++hl) {
+        const int h = hg * kHg + hl;
+        if (h >= heads) break;
+        float* o = ws + ((int64_t)rr * heads + h) * (d + 2);
+        if (t == 0) {
+            o[0] = mstate[hl];
+            o[1] = lstate[hl];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[2 + col + k] = u[hl][k];
+    }
+}
+
+// One block per head: merge the splits (u / l at the common max), then
+// out[h*hd + j] = bf16(wv[h*hd + j, :] . u + bv[h*hd + j]).
+__global__ void __launch_bounds__(kCombThreads) wide1q_combine_kernel(const float* __restrict__ ws, int splits,
+                                                                      int heads, int d, int hd,
+                                                                      const __nv_bfloat16* __restrict__ wv,
+                                                                      int64_t ldw, const __nv_bfloat16* __restrict__ bv,
+                                                                      __nv_bfloat16* __restrict__ out) {
+    extern __shared__ float ubar[];              // [d]
+    __shared__ float wsplit[1024];
+    __shared__ float inv_l;
+    const int h = blockIdx.x, t = threadIdx.x;
+    if (t == 0) {
+        float m = -INFINITY;
+        for (int s = 0; s < splits; ++s) m = fmaxf(m, ws[((int64_t)s * heads + h) * (d + 2)]);
+        float l = 0.f;
+        for (int s = 0; s < splits; ++s) {
+            const float* o = ws + ((int64_t)s * heads + h) * (d + 2);
+            const float w = o[0] == -INFINITY ? 0.f : exp2f(o[0] - m);
+            wsplit[s] = w;
+            l += w * o[1];
+        }
+        inv_l = 1.f / l;
+    }
+    __syncthreads();
+    for (int c = t; c < d; c += kCombThreads) {
+        float acc = 0.f;
+        for (int s = 0; s < splits; ++s) acc = fmaf(wsplit[s], ws[((int64_t)s * heads + h) * (d + 2) + 2 + c], acc);
+        ubar[c] = acc * inv_l;
+    }
+    __syncthreads();
+    const int warp = t >> 5, lane = t & 31;
+    for (int j = warp; j < hd; j += kCombThreads / 32) {
+        const __nv_bfloat16* w = wv + ((int64_t)h * hd + j) * ldw;
+        float acc = 0.f;
+        for (int c = lane * 8; c < d; c += 256) {
+            float wf[8];
+            load8_nc(w + c, wf);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc = fmaf(wf[k], ubar[c + k], acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) out[(int64_t)h * hd + j] = f2bf(acc + bf2f(bv[(int64_t)h * hd + j]));
+    }
+}
+
+int splits_for(int64_t n) {      // row ranges (the combine kernel merges at most 1024)
+    return (int)std::max<int64_t>(1, std::min<int64_t>(1024, (n + kRowsPerRange - 1) / kRowsPerRange));
+}
+
+}  // namespace
+}  // namespace vdit
+
+using namespace vdit;
+
+extern "C" size_t vdit_attention_1q_wide_workspace_bytes(int32_t heads, int32_t head_dim, int64_t n_keys) {
+    const int64_t d = (int64_t)heads * head_dim;
+    return (size_t)heads * (size_t)(d + 2) * sizeof(float) * (size_t)(1 + splits_for(n_keys));
+}
+
+extern "C" int vdit_attention_1q_wide(const void* q, const void* x, int64_t ldx, int64_t n, const void* wk,
+                                      const void* wv, int64_t ldw, const void* bv, int32_t heads, int32_t head_dim,
+                                      float softmax_scale, void* out, void* workspace, size_t workspace_bytes,
+                                      vdit_stream_t stream) {
+    if (!q || !x || !wk || !wv || !bv || !out || !workspace || n < 1 || heads < 1 || head_dim < 1) return VDIT_ERR_ARG;
+    const int64_t d = (int64_t)heads * head_dim;
+    if (heads > kMaxHeads || d % 128 || d > 2048 || head_dim > 256) return VDIT_ERR_UNSUPPORTED;
+    if (ldx < d || ldw < d) return VDIT_ERR_ARG;
+    if (!aligned16(x) || !aligned16(wv) || !aligned16(workspace) || ldx % 8 || ldw % 8) return VDIT_ERR_ALIGN;
+    if (workspace_bytes < vdit_attention_1q_wide_workspace_bytes(heads, head_dim, n)) return VDIT_ERR_WORKSPACE;
+    const int splits = splits_for(n);
+    float* qf = static_cast<float*>(workspace);
+    float* ws = qf + heads * d;                  // heads x d qf, then splits x heads x (d + 2)
+    ws = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(ws) + 15) & ~uintptr_t(15));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const float scale_log2 = softmax_scale * 1.4426950408889634f;
+    wide1q_fold_kernel<<<dim3((unsigned)((d + kFoldThreads - 1) / kFoldThreads), heads), kFoldThreads, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(wk), ldw, (int)d, head_dim,
+        scale_log2, qf);
+    const int threads = (int)(d / 4);            // 32..512
+    const int64_t per = (n + splits - 1) / splits;
+    const int ngroups = (heads + kHg - 1) / kHg;
+    wide1q_partial_kernel<<<(unsigned)(splits * ngroups), threads, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx,
+                                                                            n, (int)d, heads, qf, per, ws);
+    wide1q_combine_kernel<<<heads, kCombThreads, (size_t)d * sizeof(float), s>>>(
+        ws, splits, heads, (int)d, head_dim, static_cast<const __nv_bfloat16*>(wv), ldw,
+        static_cast<const __nv_bfloat16*>(bv), static_cast<__nv_bfloat16*>(out));
+    count_launches(3);
+    return check_launch();
+}

@@ -464,7 +464,9 @@ class OptimizedLatDitRunner:
             if h is not None and b < cd:
                 h_mod = fk.fast_gate_add_and_modulate(x, h, G[b, 2], G[b, 3], G[b, 4])
             if b < cd:
-                kv_x = F.linear(h_mod, w["kvx_w"], w["kvx_b"])                     # [N, 2D]
+                # the context query attends over K/V = cross linear of the modulated stream;
+                # attention_1q_wide reads the stream itself (K/V are never formed)
+                h_kv = h_mod
                 if two:
                     kv_ready = torch.cuda.Event()
                     kv_ready.record(main)
@@ -474,8 +476,8 @@ class OptimizedLatDitRunner:
                 with torch.cuda.stream(side):
                     if two:
                         side.wait_event(kv_ready)
-                        kv_x.record_stream(side)
-                    o1 = fk.attention_1q(q_cc, kv_x, H, HD)                        # bf16 [D]
+                        h_kv.record_stream(side)
+                    o1 = fk.attention_1q_wide(q_cc, h_kv, w["kvx_w"], w["kvx_b"], H, HD)   # bf16 [D]
                     fk.vec_gate_residual_(c, F.linear(o1, w["cond_to_out_cross"], w["cond_to_out_cross_b"]), CG[5])
                     a_g = mod_lin(CG[6], CG[7], "cond_ffn0", "cond_ffn0_b", w)    # bf16 [2F]
                     y = fk.fast_swiglu_from_packed(a_g.view(1, -1))                 # silu(g) * a, bf16

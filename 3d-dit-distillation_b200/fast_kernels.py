@@ -448,6 +448,28 @@ def attention_1q(q: torch.Tensor, kv: torch.Tensor, heads: int, head_dim: int,
     return out
 
 
+def attention_1q_wide(q: torch.Tensor, x: torch.Tensor, w_kv: torch.Tensor, b_kv: torch.Tensor, heads: int,
+                      head_dim: int) -> torch.Tensor:
+    """One query per head ([H*HD]) over keys K = x W_k^T + b_k and values V = x W_v^T + b_v
+    (``w_kv`` = [W_k; W_v] [2D, D], ``b_kv`` = [b_k; b_v]) without forming K and V: the
+    1-token context->x attention (``lib/fast_flow.py:1769-1777``) on the voxel rows x."""
+    d = heads * head_dim
+    if x.dtype != BF16 or x.dim() != 2 or x.shape[1] != d or x.stride(1) != 1:
+        raise ValueError(f"attention_1q_wide: x must be a bf16 [n, {d}] view")
+    if w_kv.dtype != BF16 or w_kv.shape != (2 * d, d) or not w_kv.is_contiguous() or b_kv.numel() != 2 * d:
+        raise ValueError(f"attention_1q_wide: w_kv must be contiguous bf16 [{2 * d}, {d}], b_kv [{2 * d}]")
+    n = x.shape[0]
+    ws = torch.empty(int(lib().vdit_attention_1q_wide_workspace_bytes(heads, head_dim, n)), dtype=torch.uint8,
+                     device=x.device)
+    out = torch.empty(d, dtype=BF16, device=x.device)
+    q = q.reshape(-1).to(BF16).contiguous()
+    bv = b_kv.reshape(-1)[d:].to(BF16).contiguous()
+    check(lib().vdit_attention_1q_wide(ptr(q), ptr(x), x.stride(0), n, ptr(w_kv[:d]), ptr(w_kv[d:]), w_kv.stride(0),
+                                       ptr(bv), heads, head_dim, float(1.0 / math.sqrt(head_dim)), ptr(out), ptr(ws),
+                                       ws.numel(), _s(x)), "attention_1q_wide")
+    return out
+
+
 # ----------------------------------------------------------------------------- sampler glue
 
 def gather_rows_f32(src: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:

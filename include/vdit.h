@@ -215,6 +215,21 @@ int vdit_attention_1q_noalloc(const void* q, const void* k, const void* v, int64
                               int64_t n_keys, int32_t heads, int32_t head_dim, float softmax_scale,
                               void* out, vdit_stream_t stream);
 
+/* The same single-query attention with the keys and values given as a linear of the
+ * voxel rows, K = x wk^T + bk, V = x wv^T + bv (the 1-token branch's cross linear of
+ * the modulated voxel stream, lib/fast_flow.py:1769-1777), without forming them: each
+ * query is folded through wk, x is streamed once (fp32 scores, online softmax, the
+ * probability-weighted sums of its rows), and wv, bv are applied to the merged sums
+ * (bk shifts every score of a head equally and drops out).  q bf16 [heads*head_dim];
+ * x bf16 [n, ldx]; wk, wv bf16 [heads*head_dim, ldw] (rows = output channels);
+ * bv bf16 [heads*head_dim]; out bf16 [heads*head_dim].  heads <= 16,
+ * heads*head_dim % 128 == 0 and <= 2048; workspace of
+ * vdit_attention_1q_wide_workspace_bytes bytes. */
+size_t vdit_attention_1q_wide_workspace_bytes(int32_t heads, int32_t head_dim, int64_t n_keys);
+int vdit_attention_1q_wide(const void* q, const void* x, int64_t ldx, int64_t n, const void* wk, const void* wv,
+                           int64_t ldw, const void* bv, int32_t heads, int32_t head_dim, float softmax_scale,
+                           void* out, void* workspace, size_t workspace_bytes, vdit_stream_t stream);
+
 /* ------------------------------------------------------------------ sparse conv (dense) */
 /* Dense 27-tap sparse conv on tcgen05: out[n,co] = b[co] + sum_d sum_ci
  * W[d,co,ci] f[idx[n,d],ci].  f bf16 [n,cin]; w bf16 [27,cout,cin] (the

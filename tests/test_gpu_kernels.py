@@ -470,3 +470,25 @@ def test_linear_qkv_rope3d_rejects_odd_shapes():
             fk.linear_qkv_rope3d(a, torch.zeros(3 * D, K, device=DEV, dtype=torch.bfloat16),
                                  torch.zeros(3 * D, device=DEV, dtype=torch.bfloat16), torch.ones(D, device=DEV),
                                  torch.ones(D, device=DEV), cos, sin, hc, bwd, heads, hd)
+
+
+@pytest.mark.parametrize("n,heads,hd", [(16384, 12, 128), (1, 12, 128), (777, 16, 96), (5000, 2, 128)])
+def test_attention_1q_wide(n, heads, hd):
+    """The single query over K/V = x W^T + b without forming K/V, against forming them
+    (F.linear, the bf16 K/V the reference attends over) with the single-query kernel,
+    and against fp32 math."""
+    g = torch.Generator(device=DEV).manual_seed(n + heads)
+    D = heads * hd
+    x = torch.randn(n, D, device=DEV, generator=g).to(torch.bfloat16)
+    w_kv = (0.04 * torch.randn(2 * D, D, device=DEV, generator=g)).to(torch.bfloat16)
+    b_kv = (0.3 * torch.randn(2 * D, device=DEV, generator=g)).to(torch.bfloat16)
+    q = (2.0 * torch.randn(D, device=DEV, generator=g)).to(torch.bfloat16)
+    out = fk.attention_1q_wide(q, x, w_kv, b_kv, heads, hd)
+    kv = torch.nn.functional.linear(x, w_kv, b_kv)
+    two = fk.attention_1q(q, kv, heads, hd)
+    kf = (x.float() @ w_kv[:D].float().t() + b_kv[:D].float()).view(n, heads, hd)
+    vf = (x.float() @ w_kv[D:].float().t() + b_kv[D:].float()).view(n, heads, hd)
+    p = torch.softmax(torch.einsum("hd,nhd->hn", q.float().view(heads, hd), kf) / math.sqrt(hd), dim=1)
+    ref = torch.einsum("hn,nhd->hd", p, vf).reshape(-1)
+    assert rel(out, ref) < 1e-2
+    assert rel(out, two) < 2e-2
