@@ -26,21 +26,30 @@ constexpr int kRowsPerRange = 128;
 constexpr int kFoldThreads = 256;
 constexpr int kCombThreads = 256;
 
-// qf[h, d] = scale_log2 * sum_j q[h*hd + j] * wk[(h*hd + j), d]
+// qf[h, d] = scale_log2 * sum_j q[h*hd + j] * wk[(h*hd + j), d]; a block covers 64 columns
+// of one head, its four thread groups a quarter of the j range each
 __global__ void __launch_bounds__(kFoldThreads) wide1q_fold_kernel(const __nv_bfloat16* __restrict__ q,
                                                                    const __nv_bfloat16* __restrict__ wk,
                                                                    int64_t ldw, int d, int hd, float scale_log2,
                                                                    float* __restrict__ qf) {
     __shared__ float qs[256];
+    __shared__ float part[4][64];
     const int h = blockIdx.y;
-    const int col = blockIdx.x * kFoldThreads + threadIdx.x;
+    const int c = threadIdx.x & 63, jg = threadIdx.x >> 6;
+    const int col = blockIdx.x * 64 + c;
     for (int j = threadIdx.x; j < hd; j += kFoldThreads) qs[j] = bf2f(q[(int64_t)h * hd + j]);
     __syncthreads();
-    if (col >= d) return;
-    const __nv_bfloat16* w = wk + (int64_t)h * hd * ldw + col;
+    const int j0 = jg * hd / 4, j1 = (jg + 1) * hd / 4;
     float acc = 0.f;
-    for (int j = 0; j < hd; ++j) acc = fmaf(qs[j], bf2f(w[(int64_t)j * ldw]), acc);
-    qf[(int64_t)h * d + col] = acc * scale_log2;
+    if (col < d) {
+        const __nv_bfloat16* w = wk + (int64_t)h * hd * ldw + col;
+#pragma unroll 8
+        for (int j = j0; j < j1; ++j) acc = fmaf(qs[j], bf2f(w[(int64_t)j * ldw]), acc);
+    }
+    part[jg][c] = acc;
+    __syncthreads();
+    if (jg == 0 && col < d)
+        qf[(int64_t)h * d + col] = ((part[0][c] + part[1][c]) + (part[2][c] + part[3][c])) * scale_log2;
 }
 
 // A block handles one range of rows for one group of kHg heads (the groups of a range
@@ -78,23 +87,26 @@ __global__ void wide1q_partial_kernel(const __nv_bfloat16* __restrict__ x, int64
         lstate[t] = 0.f;
     }
 
+    // raw rows of the next batch are loaded while the current one is reduced
+    uint2 nxt[kRows];
+    auto fetch = [&](int64_t b) {
+#pragma unroll
+        for (int r = 0; r < kRows; ++r)
+            nxt[r] = b + r < r1 ? __ldg(reinterpret_cast<const uint2*>(x + (b + r) * ldx + col)) : make_uint2(0u, 0u);
+    };
+    fetch(r0);
     for (int64_t b = r0; b < r1; b += kRows) {
         float hv[kRows][4];
 #pragma unroll
         for (int r = 0; r < kRows; ++r) {
-            if (b + r < r1) {
-                const uint2 raw = __ldg(reinterpret_cast<const uint2*>(x + (b + r) * ldx + col));
-                const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-                const float2 a = __bfloat1622float2(p2[0]), c = __bfloat1622float2(p2[1]);
-                hv[r][0] = a.x;
-                hv[r][1] = a.y;
-                hv[r][2] = c.x;
-                hv[r][3] = c.y;
-            } else {
-#pragma unroll
-                for (int k = 0; k < 4; ++k) hv[r][k] = 0.f;
-            }
+            const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&nxt[r]);
+            const float2 a = __bfloat1622float2(p2[0]), c = __bfloat1622float2(p2[1]);
+            hv[r][0] = a.x;
+            hv[r][1] = a.y;
+            hv[r][2] = c.x;
+            hv[r][3] = c.y;
         }
+        if (b + kRows < r1) fetch(b + kRows);
         float val[V];
 #pragma unroll
         for (int r = 0; r < kRows; ++r)
@@ -170,49 +182,76 @@ __global__ void wide1q_partial_kernel(const __nv_bfloat16* __restrict__ x, int64
     }
 }
 
-// One block per head: merge the splits (u / l at the common max), then
-// out[h*hd + j] = bf16(wv[h*hd + j, :] . u + bv[h*hd + j]).
-__global__ void __launch_bounds__(kCombThreads) wide1q_combine_kernel(const float* __restrict__ ws, int splits,
-                                                                      int heads, int d, int hd,
-                                                                      const __nv_bfloat16* __restrict__ wv,
+// Merge the row ranges of one head (u / l at the common max) for 256 columns per block:
+// ubar[h, c] = sum_s w_s u_s[c] / sum_s w_s l_s, w_s = 2^(m_s - max m).
+__global__ void __launch_bounds__(kCombThreads) wide1q_merge_kernel(const float* __restrict__ ws, int splits,
+                                                                    int heads, int d, float* __restrict__ ubar) {
+    __shared__ float wsplit[1024];
+    __shared__ float red[kCombThreads / 32];
+    __shared__ float m_all, inv_l;
+    const int h = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    float m = -INFINITY;
+    for (int s = t; s < splits; s += kCombThreads) m = fmaxf(m, ws[((int64_t)s * heads + h) * (d + 2)]);
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (t == 0) {
+        float v = red[0];
+        for (int w = 1; w < kCombThreads / 32; ++w) v = fmaxf(v, red[w]);
+        m_all = v;
+    }
+    __syncthreads();
+    float l = 0.f;
+    for (int s = t; s < splits; s += kCombThreads) {
+        const float* o = ws + ((int64_t)s * heads + h) * (d + 2);
+        const float w = o[0] == -INFINITY ? 0.f : exp2f(o[0] - m_all);
+        wsplit[s] = w;
+        l += w * o[1];
+    }
+    l = warp_sum(l);
+    __syncthreads();                 // red is reused
+    if (lane == 0) red[warp] = l;
+    __syncthreads();
+    if (t == 0) {
+        float v = 0.f;
+        for (int w = 0; w < kCombThreads / 32; ++w) v += red[w];
+        inv_l = 1.f / v;
+    }
+    __syncthreads();
+    const int c = blockIdx.x * kCombThreads + t;
+    if (c >= d) return;
+    float acc = 0.f;
+    for (int s = 0; s < splits; ++s) acc = fmaf(wsplit[s], ws[((int64_t)s * heads + h) * (d + 2) + 2 + c], acc);
+    ubar[(int64_t)h * d + c] = acc * inv_l;
+}
+
+// out[h*hd + j] = bf16(wv[h*hd + j, :] . ubar[h] + bv[h*hd + j]), one warp per output channel
+__global__ void __launch_bounds__(kCombThreads) wide1q_project_kernel(const float* __restrict__ ubar, int heads, int d,
+                                                                      int hd, const __nv_bfloat16* __restrict__ wv,
                                                                       int64_t ldw, const __nv_bfloat16* __restrict__ bv,
                                                                       __nv_bfloat16* __restrict__ out) {
-    extern __shared__ float ubar[];              // [d]
-    __shared__ float wsplit[1024];
-    __shared__ float inv_l;
-    const int h = blockIdx.x, t = threadIdx.x;
-    if (t == 0) {
-        float m = -INFINITY;
-        for (int s = 0; s < splits; ++s) m = fmaxf(m, ws[((int64_t)s * heads + h) * (d + 2)]);
-        float l = 0.f;
-        for (int s = 0; s < splits; ++s) {
-            const float* o = ws + ((int64_t)s * heads + h) * (d + 2);
-            const float w = o[0] == -INFINITY ? 0.f : exp2f(o[0] - m);
-            wsplit[s] = w;
-            l += w * o[1];
-        }
-        inv_l = 1.f / l;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t o = (int64_t)blockIdx.x * (kCombThreads / 32) + warp;     // output channel
+    if (o >= (int64_t)heads * hd) return;
+    const float* u = ubar + (o / hd) * d;
+    const __nv_bfloat16* w = wv + o * ldw;
+    float acc = 0.f;
+    for (int c = lane * 8; c < d; c += 256) {
+        float wf[8];
+        load8_nc(w + c, wf);
+        const float4 u0 = *reinterpret_cast<const float4*>(u + c);
+        const float4 u1 = *reinterpret_cast<const float4*>(u + c + 4);
+        acc = fmaf(wf[0], u0.x, acc);
+        acc = fmaf(wf[1], u0.y, acc);
+        acc = fmaf(wf[2], u0.z, acc);
+        acc = fmaf(wf[3], u0.w, acc);
+        acc = fmaf(wf[4], u1.x, acc);
+        acc = fmaf(wf[5], u1.y, acc);
+        acc = fmaf(wf[6], u1.z, acc);
+        acc = fmaf(wf[7], u1.w, acc);
     }
-    __syncthreads();
-    for (int c = t; c < d; c += kCombThreads) {
-        float acc = 0.f;
-        for (int s = 0; s < splits; ++s) acc = fmaf(wsplit[s], ws[((int64_t)s * heads + h) * (d + 2) + 2 + c], acc);
-        ubar[c] = acc * inv_l;
-    }
-    __syncthreads();
-    const int warp = t >> 5, lane = t & 31;
-    for (int j = warp; j < hd; j += kCombThreads / 32) {
-        const __nv_bfloat16* w = wv + ((int64_t)h * hd + j) * ldw;
-        float acc = 0.f;
-        for (int c = lane * 8; c < d; c += 256) {
-            float wf[8];
-            load8_nc(w + c, wf);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) acc = fmaf(wf[k], ubar[c + k], acc);
-        }
-        acc = warp_sum(acc);
-        if (lane == 0) out[(int64_t)h * hd + j] = f2bf(acc + bf2f(bv[(int64_t)h * hd + j]));
-    }
+    acc = warp_sum(acc);
+    if (lane == 0) out[o] = f2bf(acc + bf2f(bv[o]));
 }
 
 int splits_for(int64_t n) {      // row ranges (the combine kernel merges at most 1024)
@@ -226,7 +265,7 @@ using namespace vdit;
 
 extern "C" size_t vdit_attention_1q_wide_workspace_bytes(int32_t heads, int32_t head_dim, int64_t n_keys) {
     const int64_t d = (int64_t)heads * head_dim;
-    return (size_t)heads * (size_t)(d + 2) * sizeof(float) * (size_t)(1 + splits_for(n_keys));
+    return (size_t)heads * (size_t)(d + 2) * sizeof(float) * (size_t)(2 + splits_for(n_keys));
 }
 
 extern "C" int vdit_attention_1q_wide(const void* q, const void* x, int64_t ldx, int64_t n, const void* wk,
@@ -240,12 +279,12 @@ extern "C" int vdit_attention_1q_wide(const void* q, const void* x, int64_t ldx,
     if (!aligned16(x) || !aligned16(wv) || !aligned16(workspace) || ldx % 8 || ldw % 8) return VDIT_ERR_ALIGN;
     if (workspace_bytes < vdit_attention_1q_wide_workspace_bytes(heads, head_dim, n)) return VDIT_ERR_WORKSPACE;
     const int splits = splits_for(n);
-    float* qf = static_cast<float*>(workspace);
-    float* ws = qf + heads * d;                  // heads x d qf, then splits x heads x (d + 2)
-    ws = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(ws) + 15) & ~uintptr_t(15));
+    float* qf = static_cast<float*>(workspace);  // heads x d, then ubar heads x d, then splits x heads x (d + 2)
+    float* ubar = qf + heads * d;
+    float* ws = ubar + heads * d;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const float scale_log2 = softmax_scale * 1.4426950408889634f;
-    wide1q_fold_kernel<<<dim3((unsigned)((d + kFoldThreads - 1) / kFoldThreads), heads), kFoldThreads, 0, s>>>(
+    wide1q_fold_kernel<<<dim3((unsigned)((d + 63) / 64), heads), kFoldThreads, 0, s>>>(
         static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(wk), ldw, (int)d, head_dim,
         scale_log2, qf);
     const int threads = (int)(d / 4);            // 32..512
@@ -253,9 +292,13 @@ extern "C" int vdit_attention_1q_wide(const void* q, const void* x, int64_t ldx,
     const int ngroups = (heads + kHg - 1) / kHg;
     wide1q_partial_kernel<<<(unsigned)(splits * ngroups), threads, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx,
                                                                             n, (int)d, heads, qf, per, ws);
-    wide1q_combine_kernel<<<heads, kCombThreads, (size_t)d * sizeof(float), s>>>(
-        ws, splits, heads, (int)d, head_dim, static_cast<const __nv_bfloat16*>(wv), ldw,
-        static_cast<const __nv_bfloat16*>(bv), static_cast<__nv_bfloat16*>(out));
-    count_launches(3);
+    wide1q_merge_kernel<<<dim3((unsigned)((d + kCombThreads - 1) / kCombThreads), heads), kCombThreads, 0, s>>>(
+        ws, splits, heads, (int)d, ubar);
+    wide1q_project_kernel<<<(unsigned)((heads * head_dim + kCombThreads / 32 - 1) / (kCombThreads / 32)),
+                            kCombThreads, 0, s>>>(ubar, heads, (int)d, head_dim,
+                                                  static_cast<const __nv_bfloat16*>(wv), ldw,
+                                                  static_cast<const __nv_bfloat16*>(bv),
+                                                  static_cast<__nv_bfloat16*>(out));
+    count_launches(4);
     return check_launch();
 }
