@@ -1,0 +1,58 @@
+"""Build recipe for the reference's own sparse-conv CUDA kernels, a test-only checker.
+
+Compiles ``oracle/ref_libsparse.cpp`` (our binding) with the reference's unmodified
+``BK/ops/libsparse/conv.cu``, read where it lies in the reference checkout, for sm_100a
+into ``oracle/_ref/vdit_ref_libsparse.so`` (git-ignored; it travels to the GPU box with
+the other built libraries).  Skipped when the checkout is absent.  The reference's own
+build system (its setup.py, which also pulls in its attention and mesh sources) is not
+used.
+
+    python oracle/build_ref.py
+"""
+from __future__ import annotations
+
+import os
+import shutil
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+REF_CONV = Path("/root/reference/baseline_repo/3dgen-main/ops/libsparse/conv.cu")
+OUT_DIR = HERE / "_ref"
+OUT = OUT_DIR / "vdit_ref_libsparse.so"
+NAME = "vdit_ref_libsparse"
+
+
+def build(verbose: bool = False):
+    """Returns the built library's path, or None without the reference checkout."""
+    if not REF_CONV.exists():
+        return None
+    sources = [HERE / "ref_libsparse.cpp", REF_CONV]
+    if OUT.exists() and OUT.stat().st_mtime >= max(s.stat().st_mtime for s in sources):
+        return OUT
+    bdir = OUT_DIR / "build"
+    bdir.mkdir(parents=True, exist_ok=True)
+    os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0")
+    from torch.utils.cpp_extension import load
+    load(name=NAME, sources=[str(s) for s in sources], build_directory=str(bdir),
+         extra_cuda_cflags=["-O3", "-gencode", "arch=compute_100a,code=sm_100a"],
+         verbose=verbose, is_python_module=True)
+    shutil.copy2(bdir / f"{NAME}.so", OUT)
+    return OUT
+
+
+def load_built():
+    """Import the prebuilt checker module (None when it was not built)."""
+    if not OUT.exists():
+        return None
+    import importlib.machinery
+    import importlib.util
+    import torch  # noqa: F401  (the module links against torch's libraries)
+    loader = importlib.machinery.ExtensionFileLoader(NAME, str(OUT))
+    spec = importlib.util.spec_from_loader(NAME, loader)
+    mod = importlib.util.module_from_spec(spec)
+    loader.exec_module(mod)
+    return mod
+
+
+if __name__ == "__main__":
+    print(build(verbose=True))
