@@ -36,7 +36,6 @@ namespace gemm {
 using namespace tc;
 
 constexpr int BM = 128;             // rows per CTA (256 per pair)
-constexpr int BN_FULL = 256;        // output columns per pair tile (192 for the head_dim-96 qkv)
 constexpr int BK = 64;
 constexpr int EPI_WARPS = 4;
 constexpr int THREADS = (2 + EPI_WARPS) * 32;
@@ -48,13 +47,13 @@ constexpr int EPI_QKV = 1;    // self-attention qkv: QK-RMSNorm + 3D RoPE, rows 
                               // a pair tile holds two whole heads (BN = 2 * head_dim, 256 or 192)
 constexpr int kQkvTableBytes = 24576;   // EPI_QKV: RoPE cos + sin tables staged in shared memory
 
-// EPI_BIAS: a 6-stage ring and, per epilogue warp, two 32-row x 64-column bf16 boxes stored
+// EPI_BIAS: a 6-stage ring (8 for 128-column tiles) and, per epilogue warp, two 32-row x 64-column bf16 boxes stored
 // by TMA.  EPI_QKV: a 4-stage ring, the RoPE tables and, per epilogue warp, two buffers of
 // 32 head rows (one per head of the tile), padded to spread the lanes' stores over the
 // banks; each row leaves with its own bulk copy to its scattered output row.
 template <int EPI, int BN>
 struct __align__(1024) Smem {
-    static constexpr int NST = EPI == EPI_QKV ? 4 : 6;
+    static constexpr int NST = EPI == EPI_QKV ? 4 : BN == 128 ? 8 : 6;
     static constexpr int ROWPAD = BN + 16;                 // a head row: BN / 2 bf16 = BN bytes
     static constexpr int XBYTES =
         EPI == EPI_QKV ? kQkvTableBytes + EPI_WARPS * 2 * 32 * ROWPAD : EPI_WARPS * 2 * 32 * 128;
@@ -372,35 +371,52 @@ int num_sms() {
 }
 
 template <int EPI, int BN>
-int launch(const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo, int64_t m, int n, int k,
-           const EpiArgs& ep, cudaStream_t s) {
-    const size_t smem = sizeof(Smem<EPI, BN>) + 1024;
-    static int max_pairs = 0;
+cudaLaunchConfig_t launch_config(cudaLaunchAttribute* attr, cudaStream_t s) {
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.blockDim = dim3(THREADS);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = sizeof(Smem<EPI, BN>) + 1024;
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (max_pairs == 0) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    return cfg;
+}
+
+// CTA pairs of gemm_kernel<EPI, BN> resident at once on this GPU (queried once; 0 on error).
+template <int EPI, int BN>
+int max_pairs() {
+    static int pairs = 0;
+    if (pairs == 0) {
+        cudaLaunchAttribute attr[1];
+        cudaLaunchConfig_t cfg = launch_config<EPI, BN>(attr, nullptr);
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)cfg.dynamicSmemBytes);
+        int p = 0;
         if (e == cudaSuccess) {
             cfg.gridDim = dim3(2 * (num_sms() / 2));
-            e = cudaOccupancyMaxActiveClusters(&max_pairs, gemm_kernel<EPI, BN>, &cfg);
+            e = cudaOccupancyMaxActiveClusters(&p, gemm_kernel<EPI, BN>, &cfg);
         }
-        if (e != cudaSuccess || max_pairs <= 0) {
-            max_pairs = 0;
+        if (e != cudaSuccess || p <= 0) {
             record_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidConfiguration);
-            return VDIT_ERR_LAUNCH;
+            return 0;
         }
+        pairs = p;
     }
+    return pairs;
+}
+
+template <int EPI, int BN>
+int launch(const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo, int64_t m, int n, int k,
+           const EpiArgs& ep, cudaStream_t s) {
+    const int pairs = max_pairs<EPI, BN>();
+    if (pairs <= 0) return VDIT_ERR_LAUNCH;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = launch_config<EPI, BN>(attr, s);
     const int64_t ntiles = ((m + 2 * BM - 1) / (2 * BM)) * (n / BN);
-    cfg.gridDim = dim3((unsigned)(2 * std::min<int64_t>(ntiles, max_pairs)));
+    cfg.gridDim = dim3((unsigned)(2 * std::min<int64_t>(ntiles, pairs)));
     const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<EPI, BN>, ma, mw, mo, m, n, k, ep);
     if (e != cudaSuccess) {
         record_cuda_error(e);
@@ -408,6 +424,15 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo, 
     }
     count_launches(1);
     return check_launch();
+}
+
+// The pair tile width for an [m, n] output: the widest of 256, 192 and 128 columns that
+// divides n.  The mainloop is bound by shared-memory bandwidth (MMA operand reads plus TMA
+// fills: 128, 146 and 190 bytes per clock at the full MMA rate for those widths), so per
+// FLOP a 192-column tile runs 1.17x and a 128-column tile 1.5x the time of a 256-column
+// one, more than a narrower tile ever saves on a partial last round.
+int pick_bn(int n) {
+    return n % 256 == 0 ? 256 : n % 192 == 0 ? 192 : 128;
 }
 
 }  // namespace gemm
@@ -430,18 +455,22 @@ extern "C" int vdit_linear(const void* a, int64_t lda, const void* w, int64_t ld
                            int64_t ldo, int64_t m, int32_t n, int32_t k, vdit_stream_t stream) {
     using namespace vdit::gemm;
     if (!a || !w || !out || m < 0 || n <= 0 || k <= 0) return VDIT_ERR_ARG;
-    if (n % BN_FULL || k % BK) return VDIT_ERR_UNSUPPORTED;
+    if ((n % 128 && n % 192) || k % BK) return VDIT_ERR_UNSUPPORTED;
     if (lda < k || ldw < k || ldo < n) return VDIT_ERR_ARG;
     if (!aligned16(a) || !aligned16(w) || !aligned16(out) || (bias && !aligned16(bias)) || lda % 8 || ldw % 8 ||
         ldo % 8)
         return VDIT_ERR_ALIGN;
     if (m == 0) return VDIT_OK;
     if (m > (int64_t)INT32_MAX) return VDIT_ERR_UNSUPPORTED;
+    const int bn = pick_bn(n);
     CUtensorMap ma, mw, mo;
-    if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, BN_FULL / 2) || !make_map(&mo, out, m, n, ldo, 32, 64))
+    if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, bn / 2) || !make_map(&mo, out, m, n, ldo, 32, 64))
         return VDIT_ERR_DRIVER;
     EpiArgs ep{static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out), ldo};
-    return launch<EPI_BIAS, BN_FULL>(ma, mw, mo, m, n, k, ep, static_cast<cudaStream_t>(stream));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (bn == 256) return launch<EPI_BIAS, 256>(ma, mw, mo, m, n, k, ep, s);
+    if (bn == 192) return launch<EPI_BIAS, 192>(ma, mw, mo, m, n, k, ep, s);
+    return launch<EPI_BIAS, 128>(ma, mw, mo, m, n, k, ep, s);
 }
 
 extern "C" int vdit_linear_qkv_rope3d(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias,

@@ -310,7 +310,7 @@ def dense_sparse_conv3d(feat: torch.Tensor, weight_t_bf16: torch.Tensor, bias_fp
 def linear(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
            out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``F.linear(a, w, bias)`` for bf16 2D ``a`` [M, K] (row stride free) and a
-    contiguous bf16 weight [N, K] on the tcgen05 GEMM (N % 256 == 0, K % 64 == 0)."""
+    contiguous bf16 weight [N, K] on the tcgen05 GEMM (N a multiple of 128 or 192, K % 64 == 0)."""
     if a.dtype != BF16 or w.dtype != BF16 or a.dim() != 2 or w.dim() != 2 or a.shape[1] != w.shape[1]:
         raise ValueError(f"linear: a {tuple(a.shape)} {a.dtype} and w {tuple(w.shape)} {w.dtype} "
                          "must be 2D bf16 with the same K")

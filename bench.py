@@ -288,7 +288,9 @@ def gemm_bench(w, reps: int = 20):
     D = w.arch.dim
     F2 = 2 * w.arch.ffn_dim
     shapes = [("to_qkv", w.n, D, 3 * D), ("to_out", w.n, D, D), ("ffn0", w.n, D, F2),
-              ("ffn1", w.n, F2 // 2, D), ("cond_to_qkv", w.ctx_tokens, D, 3 * D)]
+              ("ffn1", w.n, F2 // 2, D), ("cond_to_qkv", w.ctx_tokens, D, 3 * D),
+              ("cond_to_out", w.ctx_tokens, D, D), ("cond_to_kv_cross", w.ctx_tokens, D, 2 * D),
+              ("cond_ffn0", w.ctx_tokens, D, F2), ("cond_ffn1", w.ctx_tokens, F2 // 2, D)]
     g = torch.Generator(device="cuda").manual_seed(9)
     s = torch.cuda.current_stream()
     res = []
@@ -311,6 +313,19 @@ def gemm_bench(w, reps: int = 20):
             ms = e0.elapsed_time(e1) / reps
             row[impl + "_ms"] = round(ms, 4)
             row[impl + "_tflops"] = round(2 * m * k * n / ms / 1e9, 1)
+            # the same launches replayed from a CUDA graph: device time without host launch gaps
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(reps):
+                    fn()
+            graph.replay()
+            torch.cuda.synchronize()
+            e0.record(s)
+            graph.replay()
+            e1.record(s)
+            torch.cuda.synchronize()
+            row[impl + "_graph_ms"] = round(e0.elapsed_time(e1) / reps, 4)
+            del graph
         ref = F.linear(a, wt, b).float()
         row["rel_l2_vs_cublas"] = float((fk.linear(a, wt, b).float() - ref).norm() / ref.norm())
         res.append(row)

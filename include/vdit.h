@@ -240,12 +240,13 @@ int vdit_dense_conv27(const void* f, int64_t n, int32_t cin, int32_t cout, const
                       const void* w, const float* b, void* out, vdit_stream_t stream);
 
 /* ------------------------------------------------------------------ block linears */
-/* out[m,n] = bf16(sum_k a[m,k] w[n,k] + bias[n]) on tcgen05 (persistent 128x256
- * tiles, fp32 accumulation in TMEM): the nn.Linear of every block projection,
- * BK/models/generators/lat_dit.py:306-345 (the reference calls cuBLAS through
- * F.linear with bf16 weights pre-cast, lib/fast_flow.py:150-163).  a bf16 [m,lda],
- * w bf16 [n,ldw], bias bf16 [n] or NULL, out bf16 [m,ldo]; n % 256 == 0,
- * k % 64 == 0, leading dimensions multiples of 8, pointers 16-byte aligned. */
+/* out[m,n] = bf16(sum_k a[m,k] w[n,k] + bias[n]) on tcgen05 (persistent CTA-pair
+ * tiles of 256 rows x 256, 192 or 128 columns, fp32 accumulation in TMEM): the
+ * nn.Linear of every block projection, BK/models/generators/lat_dit.py:306-345 (the
+ * reference calls cuBLAS through F.linear with bf16 weights pre-cast,
+ * lib/fast_flow.py:150-163).  a bf16 [m,lda], w bf16 [n,ldw], bias bf16 [n] or NULL,
+ * out bf16 [m,ldo]; n a multiple of 128 or of 192, k % 64 == 0, leading dimensions
+ * multiples of 8, pointers 16-byte aligned. */
 int vdit_linear(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias, void* out,
                 int64_t ldo, int64_t m, int32_t n, int32_t k, vdit_stream_t stream);
 

@@ -399,8 +399,12 @@ def test_dense_conv27_rejects_bad_shapes():
 
 @pytest.mark.parametrize("m,k,n,bias,strided", [(1, 64, 256, True, False), (300, 1536, 512, True, False),
                                                  (4101, 1536, 4608, True, False), (16384, 1536, 1536, False, False),
-                                                 (1000, 3840, 1536, True, True), (129, 128, 768, True, True)])
+                                                 (1000, 3840, 1536, True, True), (129, 128, 768, True, True),
+                                                 (16384, 1536, 1536, True, True), (4101, 1536, 7680, True, False),
+                                                 (5000, 256, 576, True, False), (2000, 512, 640, False, True)])
 def test_linear_matches_fp32(m, k, n, bias, strided):
+    """Pair tiles of 256, 192 or 128 columns, the widest that divides n (n = 576 takes
+    192-column tiles, n = 640 128-column tiles with the 8-stage ring)."""
     g = torch.Generator(device=DEV).manual_seed(m + k + n)
     a_full = torch.randn(m, k + (64 if strided else 0), device=DEV, generator=g).to(torch.bfloat16)
     a = a_full[:, 16:16 + k] if strided else a_full             # row stride k + 64, 32-byte offset
@@ -424,6 +428,9 @@ def test_linear_rejects_bad_shapes():
     with pytest.raises(RuntimeError, match="unsupported"):
         fk.linear(torch.zeros(10, 128, device=DEV, dtype=torch.bfloat16),
                   torch.zeros(100, 128, device=DEV, dtype=torch.bfloat16))
+    with pytest.raises(RuntimeError, match="unsupported"):          # 320: neither 128 nor 192 divides it
+        fk.linear(torch.zeros(10, 128, device=DEV, dtype=torch.bfloat16),
+                  torch.zeros(320, 128, device=DEV, dtype=torch.bfloat16))
 
 
 @pytest.mark.parametrize("n,heads,hd,res", [(3000, 12, 128, 128), (16384, 12, 128, 64), (300, 2, 128, 64),
