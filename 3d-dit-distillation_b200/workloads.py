@@ -87,3 +87,25 @@ class C4:
         dino = torch.randn(1, self.ctx_tokens, self.arch.dino_dim, generator=g).to(torch.float16)
         return {"vox": vox.to(device), "context": ctx.to(device, torch.bfloat16), "noise": noise.to(device),
                 "vox_host": vox, "dino_host": dino, "noise_host": noise}
+
+
+@dataclass
+class C5:
+    """Sharded batch: 16 independent samples, each N=32768 voxels from a seeded union of
+    1-3 random ellipsoid shells in 128^3 with a [4101, 1536] N(0,1) context, through the
+    same 24-block DiT (RoPE resolution 128) and 4-step exact solver as C4."""
+    n: int = 32768
+    grid: int = 128
+    samples: int = 16
+    ctx_tokens: int = 4101
+    guidance: float = 3.0
+
+    arch = LatDitArch(dim=1536, head_dim=128, depth=24, cond_depth=8, res=128, patch_size=4096)
+
+    def inputs(self, seed: int, device) -> dict:
+        vox = torch.from_numpy(ellipsoid_union(self.n, self.grid, seed))
+        g = torch.Generator(device="cpu").manual_seed(seed + 1)
+        ctx = torch.randn(self.ctx_tokens, self.arch.dim, generator=g)
+        noise = torch.randn(self.n, self.arch.latent_dim, generator=g)
+        return {"vox": vox.to(device), "context": ctx.to(device, torch.bfloat16), "noise": noise.to(device)}
+

@@ -473,6 +473,68 @@ def graph_bench(w, reps: int = 5):
     return out
 
 
+def c5_bench(args, rank: int, ws: int, dev, dist):
+    """The sharded batch: ``--samples`` C5 samples (N=32768 ellipsoid-union voxels in 128^3,
+    default 16) split round-robin over the ranks, latents gathered to rank 0 over NCCL.
+    One step processes the whole batch once (strong scaling: the batch is fixed, the
+    ranks share it); device time from CUDA events, max over ranks."""
+    from vdit import _lib
+    from vdit import distributed as vd
+    from vdit.fast_sampler import SolverConfig
+    from vdit.model import LatDitModel
+    from vdit.solution import Solution
+    from vdit.workloads import C5
+    w = C5()
+    samples = args.samples or w.samples
+    if samples % ws:
+        raise SystemExit(f"--samples {samples} does not split evenly over {ws} ranks")
+    model = LatDitModel.random(w.arch, seed=0, device=dev)
+    solver = SolverConfig(num_inference_steps=4, n_guided_steps=3, n_unguided_steps=1, guidance_scale=w.guidance)
+    runner = Solution(model, solver_config=solver, device=dev).runner
+    inps = [w.inputs(seed=500 + i, device=dev) for i in range(rank, samples, ws)]
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+
+    def step():
+        lats = [runner.sample_with_context(i["vox"], i["context"], noise=i["noise"]) for i in inps]
+        if dist is not None:
+            vd.gather_latents(lats, rank, ws)
+
+    for _ in range(args.warmup):
+        step()
+    s = torch.cuda.current_stream()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    launches0 = _lib.launch_count()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for i in range(args.steps):
+            _l2_flush(flush)
+            evs[i][0].record(s)
+            step()
+            evs[i][1].record(s)
+        torch.cuda.synchronize()
+    launches = (_lib.launch_count() - launches0) // max(args.steps, 1)
+    t = torch.tensor([sum(a.elapsed_time(b) for a, b in evs) / args.steps], device=dev)
+    if dist is not None:
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = float(t.item())
+    assert _lib.device_error() == 0, "device error word set during the benchmark"
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": samples * NFE_PER_SAMPLE * w.n / (ms_step / 1e3), "unit": UNIT,
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "strong", "samples_per_s": samples / (ms_step / 1e3),
+            "ms_per_sample_per_gpu": ms_step * ws / samples, "dtype": "bf16",
+            "data": "synthetic (seeded ellipsoid-union voxels, N(0,1) context, random-init weights)",
+            "config": {"workload": f"C5 sharded batch: {samples} samples x N={w.n} (1-3 ellipsoid shells in "
+                                   f"{w.grid}^3), 24-block DiT, 4101x1536 context, 4-step exact solver = 7 NFE each",
+                       "global_batch": samples, "seq_len": w.n, "parallelism": f"samples x{ws}",
+                       "l2": "256 MiB L2 flush before every timed step"},
+            "gpu_launches": int(launches), "clocks": clk.summary()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -482,8 +544,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="one warm-up sample, then one sample inside the NVTX range 'profile_step' (for ncu)")
-    ap.add_argument("--only", choices=["attention", "dwconv", "dense_conv", "qknorm", "gate_add", "graph", "gemm", "branch_split"], default=None,
-                    help="run only one kernel on the workload's shapes (small ncu case)")
+    ap.add_argument("--only", choices=["attention", "dwconv", "dense_conv", "qknorm", "gate_add", "graph", "gemm", "branch_split",
+                                       "c5"], default=None,
+                    help="run only one kernel on the workload's shapes (small ncu case); c5: the sharded batch")
+    ap.add_argument("--samples", type=int, default=0, help="--only c5: batch size (default 16)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -503,6 +567,11 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     w = C4()
+    if args.only == "c5":
+        c5_bench(args, rank, ws, dev, dist)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
     if args.only == "attention":
         flops, ms = attention_roofline(w, None)
         print(json.dumps({"kernel": "fmha_fwd_kernel<128>", "ms_per_launch": ms, "tflops": flops / ms / 1e9}))
