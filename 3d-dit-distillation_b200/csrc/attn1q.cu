@@ -148,10 +148,9 @@ extern "C" int vdit_attention_1q(const void* q, const void* k, const void* v, in
 
 // ---------------------------------------------------------------- allocation-free variant
 // Some callers cannot allocate device memory at the point where they run this
-// kernel: code being captured into a CUDA graph (an allocation inside capture
-// is either forbidden or baked into the graph), foreign-language hosts that
-// reach the library through a plain FFI and have no device allocator of their
-// own, and serving loops that must not touch the allocator between requests.
+// kernel: foreign-language hosts that reach the library through a plain FFI
+// and have no device allocator of their own, and serving loops that must not
+// touch the allocator between requests.
 // For them vdit_attention_1q_noalloc keeps the split-K partials in a fixed
 // file-scope device array instead of a caller workspace.  The array exists
 // once per GPU that loads the library and lives until the process exits.

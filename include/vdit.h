@@ -201,8 +201,8 @@ int vdit_attention_1q(const void* q, const void* k, const void* v, int64_t kv_st
                       void* out, void* workspace, size_t workspace_bytes, vdit_stream_t stream);
 
 /* Same computation as vdit_attention_1q, for callers that cannot allocate
- * device memory (a region being captured into a CUDA graph, an FFI host with no
- * device allocator, a serving loop that must not touch the allocator).  No
+ * device memory (an FFI host with no device allocator of its own, a serving loop
+ * that must not touch the allocator between requests).  No
  * counterpart in the reference: it is an addition of this library.  The split-K
  * partials live in a fixed 1 MiB device array inside the library (one per GPU
  * that loads it, kept until process exit); heads * splits * (head_dim + 2) fp32

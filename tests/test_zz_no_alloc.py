@@ -1,7 +1,7 @@
 """The allocation-free single-query attention entry point.
 
-Callers that cannot allocate device memory where they run (graph capture, FFI
-hosts without a device allocator, serving loops kept off the allocator) call
+Callers that cannot allocate device memory where they run (FFI hosts without a
+device allocator of their own, serving loops kept off the allocator) call
 ``vdit_attention_1q_noalloc``; its split-K partials live in a fixed device
 array inside the library instead of a workspace.  This checks it through the
 C ABI against ``vdit_attention_1q`` (caller workspace) on two calls in a row,
