@@ -225,6 +225,17 @@ __global__ void __launch_bounds__(kGaMaxWarps * 32, 1) gate_add_modulate_staged_
             const float4 g0 = *reinterpret_cast<const float4*>(pg + vi * 8);
             const float4 g1 = *reinterpret_cast<const float4*>(pg + vi * 8 + 4);
             const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+            float cc[8], gc[8];              // second residual's row and gate (16-byte reads)
+            if (c2) {
+                const float4 c0 = *reinterpret_cast<const float4*>(pc2 + vi * 8);
+                const float4 c1 = *reinterpret_cast<const float4*>(pc2 + vi * 8 + 4);
+                const float4 q0 = *reinterpret_cast<const float4*>(pg2 + vi * 8);
+                const float4 q1 = *reinterpret_cast<const float4*>(pg2 + vi * 8 + 4);
+                cc[0] = c0.x; cc[1] = c0.y; cc[2] = c0.z; cc[3] = c0.w;
+                cc[4] = c1.x; cc[5] = c1.y; cc[6] = c1.z; cc[7] = c1.w;
+                gc[0] = q0.x; gc[1] = q0.y; gc[2] = q0.z; gc[3] = q0.w;
+                gc[4] = q1.x; gc[5] = q1.y; gc[6] = q1.z; gc[7] = q1.w;
+            }
             uint4 packed;
             __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&packed);
 #pragma unroll
@@ -233,8 +244,7 @@ __global__ void __launch_bounds__(kGaMaxWarps * 32, 1) gate_add_modulate_staged_
                                               xv[2 * j + 1] + hv[2 * j + 1] * gg[2 * j + 1]);
                 float2 t = __bfloat1622float2(p2[j]);
                 if (c2) {   // second residual, rounded like a second gate-add pass
-                    const int e = vi * 8 + 2 * j;
-                    p2[j] = __floats2bfloat162_rn(t.x + pc2[e] * pg2[e], t.y + pc2[e + 1] * pg2[e + 1]);
+                    p2[j] = __floats2bfloat162_rn(t.x + cc[2 * j] * gc[2 * j], t.y + cc[2 * j + 1] * gc[2 * j + 1]);
                     t = __bfloat1622float2(p2[j]);
                 }
                 r.v[i][2 * j] = t.x;
@@ -271,48 +281,129 @@ __global__ void __launch_bounds__(kGaMaxWarps * 32, 1) gate_add_modulate_staged_
     }
 }
 
-// out[row, o] = sum_c bf16(LN(x)*s1+sh)[c] * w[o, c], 16 outputs, fp32
-__global__ void __launch_bounds__(256) out_unpatchify_kernel(const __nv_bfloat16* __restrict__ x, int64_t m, int d,
-                                                             const float* __restrict__ s1, const float* __restrict__ sh,
-                                                             const float* __restrict__ w, float* __restrict__ out) {
-    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int64_t row = blockIdx.x * (int64_t)kRowWarps + warp;
-    if (row >= m) return;
-    int nvec = d >> 3;
-    RowRegs r;
-    row_load(x + row * d, nvec, lane, r);
-    float mean, rstd;
-    row_stats(r, nvec, lane, d, mean, rstd);
+// out[row, o] = sum_c bf16(LN(x)*s1+sh)[c] * w[o, c], 16 outputs, fp32.  The weight
+// (16 x d fp32) is staged in shared memory once per CTA, split so that the lanes'
+// 16-byte reads are consecutive (no bank conflicts): float4 slot (2o + h) * nvec + vi
+// holds w[o, 8vi + 4h .. 8vi + 4h + 3].  A warp takes two rows at a time, so one pass over
+// the weight serves both; lane l holds channels 8(l + 32i) .. +7 of each row.  The 2 x 16
+// per-lane partial sums are reduced by a butterfly that halves the values a lane keeps at
+// every step (the additions pair up as in warp_sum), leaving output o of row k of the pair
+// in lane 16k + o, so the two rows' 32 outputs leave in one 128-byte store.
+constexpr int kUnpRows = 2;
+constexpr int kUnpWarps = 8;
+
+__global__ void __launch_bounds__(kUnpWarps * 32) out_unpatchify_kernel(
+        const __nv_bfloat16* __restrict__ x, int64_t m, int d, const float* __restrict__ s1,
+        const float* __restrict__ sh, const float* __restrict__ w, float* __restrict__ out) {
+    extern __shared__ float4 w_s[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nvec = d >> 3, d4 = d >> 2;
+    // staging: each thread issues a batch of loads before it stores any of them
+    constexpr int kStageBatch = 12;
+    for (int q0 = tid; q0 < 16 * d4; q0 += kUnpWarps * 32 * kStageBatch) {
+        float4 t[kStageBatch];
 #pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
-        int vi = lane + 32 * i;
-        if (vi >= nvec) continue;
+        for (int b = 0; b < kStageBatch; ++b) {
+            const int q = q0 + b * kUnpWarps * 32;
+            if (q < 16 * d4) t[b] = __ldg(reinterpret_cast<const float4*>(w) + q);
+        }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            float y = (r.v[i][j] - mean) * rstd * __ldg(s1 + vi * 8 + j) + __ldg(sh + vi * 8 + j);
-            r.v[i][j] = bf2f(f2bf(y));
+        for (int b = 0; b < kStageBatch; ++b) {
+            const int q = q0 + b * kUnpWarps * 32;
+            if (q >= 16 * d4) break;
+            const int o = q / d4, c4 = q - o * d4;
+            w_s[(o * 2 + (c4 & 1)) * nvec + (c4 >> 1)] = t[b];
         }
     }
-    float acc[16];
+    __syncthreads();
+    const int64_t groups = (m + kUnpRows - 1) / kUnpRows;
+    for (int64_t gi = (int64_t)blockIdx.x * kUnpWarps + warp; gi < groups; gi += (int64_t)gridDim.x * kUnpWarps) {
+        const int64_t r0 = gi * kUnpRows;
+        uint4 y[kUnpRows][kMaxVec];          // the rows, then their modulated values, as bf16
 #pragma unroll
-    for (int o = 0; o < 16; ++o) {
-        float s = 0.f;
+        for (int k = 0; k < kUnpRows; ++k) {     // both rows' loads in flight together
+            const uint4* xr = reinterpret_cast<const uint4*>(x + (r0 + k) * d);
+#pragma unroll
+            for (int i = 0; i < kMaxVec; ++i) {
+                const int vi = lane + 32 * i;
+                y[k][i] = (r0 + k < m && vi < nvec) ? __ldg(xr + vi) : make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kUnpRows; ++k) {
+            if (r0 + k >= m) continue;       // warp-uniform: the pair's second row past m (zeros)
+            // LayerNorm statistics in the order of row_stats (same sums, same result)
+            float sum = 0.f;
+#pragma unroll
+            for (int i = 0; i < kMaxVec; ++i) {
+                if (lane + 32 * i >= nvec) continue;
+                float v[8];
+                unpack8(y[k][i], v);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) sum += v[j];
+            }
+            const float mean = warp_sum(sum) / (float)d;
+            float sq = 0.f;
+#pragma unroll
+            for (int i = 0; i < kMaxVec; ++i) {
+                if (lane + 32 * i >= nvec) continue;
+                float v[8];
+                unpack8(y[k][i], v);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) { const float t = v[j] - mean; sq += t * t; }
+            }
+            const float rstd = rsqrtf(warp_sum(sq) / (float)d + 1e-6f);
+#pragma unroll
+            for (int i = 0; i < kMaxVec; ++i) {
+                const int vi = lane + 32 * i;
+                if (vi >= nvec) continue;
+                float v[8];
+                unpack8(y[k][i], v);
+                const float4 a0 = __ldg(reinterpret_cast<const float4*>(s1 + vi * 8));
+                const float4 a1 = __ldg(reinterpret_cast<const float4*>(s1 + vi * 8 + 4));
+                const float4 b0 = __ldg(reinterpret_cast<const float4*>(sh + vi * 8));
+                const float4 b1 = __ldg(reinterpret_cast<const float4*>(sh + vi * 8 + 4));
+                const float sa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const float sb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = (v[j] - mean) * rstd * sa[j] + sb[j];
+                y[k][i] = pack8(v);
+            }
+        }
+        float acc[kUnpRows * 16];
+#pragma unroll
+        for (int t = 0; t < kUnpRows * 16; ++t) acc[t] = 0.f;
 #pragma unroll
         for (int i = 0; i < kMaxVec; ++i) {
-            int vi = lane + 32 * i;
+            const int vi = lane + 32 * i;
             if (vi >= nvec) continue;
-            const float4* wp = reinterpret_cast<const float4*>(w + (int64_t)o * d + vi * 8);
-            float4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
-            s += r.v[i][0] * w0.x + r.v[i][1] * w0.y + r.v[i][2] * w0.z + r.v[i][3] * w0.w +
-                 r.v[i][4] * w1.x + r.v[i][5] * w1.y + r.v[i][6] * w1.z + r.v[i][7] * w1.w;
-        }
-        acc[o] = warp_sum(s);
-    }
-    if (lane < 16) {
-        float v = acc[0];
+            float yv[kUnpRows][8];
 #pragma unroll
-        for (int o = 1; o < 16; ++o) if (lane == o) v = acc[o];
-        out[row * 16 + lane] = v;
+            for (int k = 0; k < kUnpRows; ++k) unpack8(y[k][i], yv[k]);
+#pragma unroll
+            for (int o = 0; o < 16; ++o) {
+                const float4 w0 = w_s[(2 * o) * nvec + vi], w1 = w_s[(2 * o + 1) * nvec + vi];
+                const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int k = 0; k < kUnpRows; ++k)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[k * 16 + o] = fmaf(yv[k][j], wv[j], acc[k * 16 + o]);
+            }
+        }
+        // reduce-scatter: after the step with offset `off`, a lane keeps the half of its
+        // values whose index has the lane's `off` bit
+#pragma unroll
+        for (int off = 16, nkeep = 16; off >= 1; off >>= 1, nkeep >>= 1) {
+            const bool upper = (lane & off) != 0;
+#pragma unroll
+            for (int j = 0; j < nkeep; ++j) {
+                const float send = upper ? acc[j] : acc[j + nkeep];
+                const float keep = upper ? acc[j + nkeep] : acc[j];
+                acc[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+            }
+        }
+        const int64_t row = r0 + (lane >> 4);
+        if (row < m) out[row * 16 + (lane & 15)] = acc[0];
     }
 }
 
@@ -502,36 +593,59 @@ __global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ h, int64_t m, in
 // their 64x16 weights sit in registers (lane = one output channel pair), each
 // warp streams rows, reading a row's 16 inputs once (broadcast) and writing
 // 64 outputs per row.
-constexpr int kPatchRows = 64;
+// x[r, c] = sum_i xt[r, i] * w[c, i] (16 inputs, fp32 FMAs in order i = 0..15), bf16 out.
+// A CTA takes 64 output channels (lane l: channels c0 = 64 bx + 2l and c0 + 1, their 32
+// weights in registers) of kPatchRows rows: the rows' xt (64 bytes each) is staged in
+// shared memory by one round of 16-byte loads issued by all threads, then each warp
+// computes every eighth row with packed FMAs (both channels in one fp32x2 FMA).
+constexpr int kPatchRows = 512;
 
 __global__ void __launch_bounds__(256) patchify_kernel(const float* __restrict__ xt, int64_t n,
                                                        const float* __restrict__ w, int d,
                                                        __nv_bfloat16* __restrict__ out) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int c0 = blockIdx.x * 64 + lane * 2;             // this lane's two output channels
-    if (c0 >= d) return;
-    float wa[16], wb[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        wa[i] = __ldg(w + (int64_t)c0 * 16 + i);
-        wb[i] = __ldg(w + (int64_t)(c0 + 1) * 16 + i);
-    }
+    __shared__ float4 xs[kPatchRows * 4];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t r0 = (int64_t)blockIdx.y * kPatchRows;
-    for (int64_t r = r0 + warp; r < min(n, r0 + kPatchRows); r += 8) {
-        const float4* xp = reinterpret_cast<const float4*>(xt + r * 16);
-        float x[16];
+    const int rows = (int)(n - r0 < kPatchRows ? n - r0 : (int64_t)kPatchRows);
+    const float4* src = reinterpret_cast<const float4*>(xt + r0 * 16);
+    float4 t[kPatchRows * 4 / 256];          // every load in flight before the first store
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float4 q = __ldg(xp + i);
-            x[4 * i] = q.x; x[4 * i + 1] = q.y; x[4 * i + 2] = q.z; x[4 * i + 3] = q.w;
-        }
-        float sa = 0.f, sb = 0.f;
+    for (int b = 0; b < kPatchRows * 4 / 256; ++b) {
+        const int q = tid + b * 256;
+        if (q < rows * 4) t[b] = __ldg(src + q);
+    }
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            sa = fmaf(x[i], wa[i], sa);
-            sb = fmaf(x[i], wb[i], sb);
+    for (int b = 0; b < kPatchRows * 4 / 256; ++b) {
+        const int q = tid + b * 256;
+        if (q < rows * 4) xs[q] = t[b];
+    }
+    const int c0 = blockIdx.x * 64 + lane * 2;
+    float2 wv[16];
+    if (c0 < d) {
+        const float4* wa = reinterpret_cast<const float4*>(w + (int64_t)c0 * 16);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 a = __ldg(wa + q), b = __ldg(wa + 4 + q);   // rows c0 and c0 + 1
+            wv[4 * q + 0] = make_float2(a.x, b.x);
+            wv[4 * q + 1] = make_float2(a.y, b.y);
+            wv[4 * q + 2] = make_float2(a.z, b.z);
+            wv[4 * q + 3] = make_float2(a.w, b.w);
         }
-        *reinterpret_cast<__nv_bfloat162*>(out + r * d + c0) = __floats2bfloat162_rn(sa, sb);
+    }
+    __syncthreads();
+    if (c0 >= d) return;
+#pragma unroll 2
+    for (int r = warp; r < rows; r += 8) {
+        float xv[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 t = xs[r * 4 + q];
+            xv[4 * q] = t.x; xv[4 * q + 1] = t.y; xv[4 * q + 2] = t.z; xv[4 * q + 3] = t.w;
+        }
+        float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc = tc::ffma2v(make_float2(xv[i], xv[i]), wv[i], acc);
+        *reinterpret_cast<__nv_bfloat162*>(out + (r0 + r) * d + c0) = __floats2bfloat162_rn(acc.x, acc.y);
     }
 }
 
@@ -678,7 +792,32 @@ extern "C" int vdit_out_modulate_unpatchify(const void* x, int64_t m, int32_t d,
     if (m < 0 || !row_width_ok(d) || !x || !s1 || !sh || !w || !out) return VDIT_ERR_ARG;
     if (!aligned16(x) || !aligned16(w) || !aligned16(s1) || !aligned16(sh)) return VDIT_ERR_ALIGN;
     if (m == 0) return VDIT_OK;
-    out_unpatchify_kernel<<<blocks_for(m, kRowWarps), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+    static int sms[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) {
+        if (e != cudaSuccess) record_cuda_error(e);
+        return VDIT_ERR_LAUNCH;
+    }
+    const size_t smem = (size_t)16 * d * sizeof(float);      // the staged weight (<= 128 KB)
+    constexpr int kMaxUnpSmem = 16 * 256 * kMaxVec * (int)sizeof(float);
+    if (sms[dev] == 0) {
+        int n = 0, per_sm = 0;
+        e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(out_unpatchify_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxUnpSmem);
+        if (e == cudaSuccess)   // resident CTAs per SM at the largest weight (registers limit it to one)
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, out_unpatchify_kernel, kUnpWarps * 32,
+                                                              kMaxUnpSmem);
+        if (e != cudaSuccess || per_sm < 1) {
+            record_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidConfiguration);
+            return VDIT_ERR_LAUNCH;
+        }
+        sms[dev] = n * per_sm;
+    }
+    const int64_t groups = (m + kUnpRows - 1) / kUnpRows;
+    const unsigned grid = (unsigned)std::min<int64_t>((groups + kUnpWarps - 1) / kUnpWarps, (int64_t)sms[dev]);
+    out_unpatchify_kernel<<<grid, kUnpWarps * 32, smem, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16*>(x), m, d, s1, sh, w, out);
     count_launches(1);
     return check_launch();

@@ -279,6 +279,92 @@ def gate_add_bench(w, reps: int = 20):
     return {"kernel": "gate_add_modulate", "ms_per_launch": ms, "gbs": 4 * w.n * D * 2 / ms / 1e6}
 
 
+def hbm_bench(w, reps: int = 10):
+    """The HBM-bound kernels of the path on the workload's shapes (N=16384 voxels, D=1536,
+    12x128 heads; geometry at N=262144 uniform voxels in 128^3).  Each launch is timed
+    alone with CUDA events after a 256 MiB L2 flush; median of ``reps`` launches after two
+    warm-up launches.  Algorithmic bytes (each tensor counted once):
+    gate-add + LN + AdaLN 4*N*D*2; LN + AdaLN 2*N*D*2; QK-norm/RoPE/gather 2*3*N*D*2 + 8N;
+    out-modulate-unpatchify N*D*2 + N*16*4; patchify N*16*4 + N*D*2; single query over
+    formed K/V 2*N*D*2; single query over the voxel rows N*D*2 + 2*D*D*2 (W_k, W_v)."""
+    from vdit import fast_kernels as fk
+    from vdit.workloads import shell_voxels, uniform_voxels
+    hbm, _, kind = _peaks()
+    n, D, H, HD = w.n, w.arch.dim, w.arch.heads, w.arch.head_dim
+    g = torch.Generator(device="cuda").manual_seed(11)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    s = torch.cuda.current_stream()
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        ms = []
+        for _ in range(reps):
+            _l2_flush(flush)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            fn()
+            e1.record(s)
+            torch.cuda.synchronize()
+            ms.append(e0.elapsed_time(e1))
+        return statistics.median(ms)
+
+    def row(name, kernel, fn, byts=None):
+        ms = timed(fn)
+        r = {"op": name, "kernel": kernel, "ms": round(ms, 4)}
+        if byts is not None:
+            r.update({"bytes": int(byts), "gbs": round(byts / ms / 1e6, 1),
+                      "frac_hbm": round(byts / ms / 1e6 / hbm, 3), "peak": f"{hbm} GB/s ({kind})"})
+        return r
+
+    bf = torch.bfloat16
+    x = torch.randn(n, D, device="cuda", generator=g).to(bf)
+    h = torch.randn(n, D, device="cuda", generator=g).to(bf)
+    gt, s1, sh, g2 = [torch.randn(D, device="cuda", generator=g) * 0.1 for _ in range(4)]
+    crow = torch.randn(D, device="cuda", generator=g).to(bf)
+    mod = torch.empty_like(x)
+    out = []
+    out.append(row("gate-add + LN + AdaLN", "gate_add_modulate_staged_kernel",
+                   lambda: fk.fast_gate_add_and_modulate(x, h, gt, s1, sh, out=mod), 4 * n * D * 2))
+    out.append(row("LN + AdaLN", "gate_add_modulate_staged_kernel (no residual)",
+                   lambda: fk.fast_modulate(x, None, s1, sh, out=mod), 2 * n * D * 2))
+    out.append(row("two gate-adds + LN + AdaLN (1-token branch)", "gate_add_modulate_staged_kernel (c2, g2)",
+                   lambda: fk.fast_gate_add2_and_modulate(x, h, gt, crow, g2, s1, sh, out=mod), 4 * n * D * 2))
+    vox = torch.from_numpy(shell_voxels(n, w.grid, w.radius, 0)).cuda()
+    _, _, hc = fk.lex_perm(vox)
+    fwd, _ = fk.hilbert4_orders(hc, 1024)
+    cos, sin = fk.precompute_rope_3d_table(w.grid, 128.0, HD, device="cuda")
+    qkv = torch.randn(n, 3 * D, device="cuda", generator=g).to(bf)
+    qkv_o = torch.empty_like(qkv)
+    qs = torch.ones(H, HD, device="cuda")
+    out.append(row("QK-RMSNorm + RoPE3D + window gather (separate pass)", "qknorm_rope_kernel<0>",
+                   lambda: fk.fused_qknorm_rope3d_gather(qkv, qs, qs, cos, sin, hc, fwd[0], H, HD, out=qkv_o),
+                   2 * 3 * n * D * 2 + 8 * n))
+    wu = torch.randn(16, D, device="cuda", generator=g) * 0.02
+    out.append(row("out LN + AdaLN + unpatchify", "out_unpatchify_kernel",
+                   lambda: fk.fast_out_modulate_unpatchify(x, None, s1, sh, wu), n * D * 2 + n * 16 * 4))
+    xt = torch.randn(n, 16, device="cuda", generator=g)
+    wp = torch.randn(D, 16, device="cuda", generator=g) * 0.02
+    out.append(row("patchify", "patchify_kernel", lambda: fk.patchify(xt, wp), n * 16 * 4 + n * D * 2))
+    q = torch.randn(D, device="cuda", generator=g)
+    kv = torch.randn(n, 2 * D, device="cuda", generator=g).to(bf)
+    out.append(row("single query over formed K/V", "attn1q_partial_kernel + attn1q_combine_kernel",
+                   lambda: fk.attention_1q(q, kv, H, HD), 2 * n * D * 2))
+    wkv = (torch.randn(2 * D, D, device="cuda", generator=g) * 0.02).to(bf)
+    bkv = (torch.randn(2 * D, device="cuda", generator=g) * 0.02).to(bf)
+    out.append(row("single query over the voxel rows (K/V not formed)", "wide1q_fold/partial/merge/project",
+                   lambda: fk.attention_1q_wide(q, x, wkv, bkv, H, HD), n * D * 2 + 2 * D * D * 2))
+    # per-sample geometry at the largest C2 size (sort-dominated; times only)
+    big = torch.from_numpy(uniform_voxels(262144, 128, 1)).cuda()
+    _, _, hcb = fk.lex_perm(big)
+    out.append(row("lexicographic order (N=262144)", "vdit_lex_perm", lambda: fk.lex_perm(big)))
+    out.append(row("four Hilbert orders + windows (N=262144)", "vdit_hilbert4_orders",
+                   lambda: fk.hilbert4_orders(hcb, 1024)))
+    out.append(row("conv_indices (N=262144)", "conv_indices_kernel",
+                   lambda: fk.build_conv_indices_fast(hcb, already_sorted=True)))
+    return out
+
+
 def gemm_bench(w, reps: int = 20):
     """The block linears of the workload (M = N voxels or the L context rows, bf16
     in/out, fp32 accumulation): the tcgen05 GEMM beside cuBLAS (``F.linear``), same
@@ -545,9 +631,10 @@ def main():
     ap.add_argument("--profile", action="store_true",
                     help="one warm-up sample, then one sample inside the NVTX range 'profile_step' (for ncu)")
     ap.add_argument("--only", choices=["attention", "dwconv", "dense_conv", "qknorm", "gate_add", "graph", "gemm", "branch_split",
-                                       "c5"], default=None,
+                                       "c5", "hbm"], default=None,
                     help="run only one kernel on the workload's shapes (small ncu case); c5: the sharded batch")
     ap.add_argument("--samples", type=int, default=0, help="--only c5: batch size (default 16)")
+    ap.add_argument("--reps", type=int, default=10, help="--only hbm: timed launches per kernel")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -581,6 +668,10 @@ def main():
         return
     if args.only == "gate_add":
         print(json.dumps(gate_add_bench(w)))
+        return
+    if args.only == "hbm":
+        for r in hbm_bench(w, reps=args.reps):
+            print(json.dumps(r))
         return
     if args.only == "branch_split":
         if ws != 2:

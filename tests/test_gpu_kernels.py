@@ -152,22 +152,32 @@ def test_gate_add_staged_matches_rowwise(m, d, stride_h):
     assert torch.equal(mod_s, mod_r)
 
 
-def test_out_modulate_unpatchify():
-    g = torch.Generator(device=DEV).manual_seed(3)
-    x = torch.randn(777, 1536, device=DEV, generator=g).to(torch.bfloat16)
-    s1 = 1 + 0.1 * torch.randn(1536, device=DEV, generator=g)
-    sh = 0.1 * torch.randn(1536, device=DEV, generator=g)
-    w = 0.05 * torch.randn(16, 1536, device=DEV, generator=g)
+@pytest.mark.parametrize("m,d", [(777, 1536), (1, 1536), (16384, 1536), (301, 1000), (64, 2048)])
+def test_out_modulate_unpatchify(m, d):
+    """Rows in pairs (odd m leaves a half pair), d not a multiple of 256 leaves lanes idle."""
+    g = torch.Generator(device=DEV).manual_seed(3 + m + d)
+    x = torch.randn(m, d, device=DEV, generator=g).to(torch.bfloat16)
+    s1 = 1 + 0.1 * torch.randn(d, device=DEV, generator=g)
+    sh = 0.1 * torch.randn(d, device=DEV, generator=g)
+    w = 0.05 * torch.randn(16, d, device=DEV, generator=g)
     out = fk.fast_out_modulate_unpatchify(x, None, s1, sh, w)
-    ref = (om.layer_norm(x.float()) * s1 + sh) @ w.t()
-    assert out.dtype == torch.float32 and rel(out, ref) < 5e-3
+    mod = (om.layer_norm(x.float()) * s1 + sh).to(torch.bfloat16).float()   # rounded as the reference does
+    ref = mod @ w.t()
+    assert out.dtype == torch.float32 and out.shape == (m, 16) and rel(out, ref) < 1e-4
+    for r in (0, m - 1):                                                    # each row on its own
+        assert rel(out[r], ref[r]) < 1e-4
 
 
-def test_patchify():
-    g = torch.Generator(device=DEV).manual_seed(4)
-    xt = torch.randn(500, 16, device=DEV, generator=g)
-    w = torch.randn(1536, 16, device=DEV, generator=g) * 0.2
-    assert rel(fk.patchify(xt, w), xt @ w.t()) < 5e-3
+@pytest.mark.parametrize("n,d", [(500, 1536), (16384, 1536), (1, 64), (1025, 200)])
+def test_patchify(n, d):
+    """Ragged row tiles (n % 512) and a channel tile with idle lanes (d = 200)."""
+    g = torch.Generator(device=DEV).manual_seed(4 + n)
+    xt = torch.randn(n, 16, device=DEV, generator=g)
+    w = torch.randn(d, 16, device=DEV, generator=g) * 0.2
+    out = fk.patchify(xt, w)
+    ref = (xt.double() @ w.double().t()).float()
+    assert out.shape == (n, d) and rel(out, ref) < 5e-3
+    assert (out.float() - ref).abs().max() <= 2 ** -7 * ref.abs().max() + 1e-6   # bf16 rounding only
 
 
 @pytest.mark.parametrize("heads,hd,res", [(12, 128, 128), (16, 96, 64), (2, 96, 64)])
