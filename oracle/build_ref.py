@@ -2,7 +2,7 @@
 
 Compiles ``oracle/ref_libsparse.cpp`` (our binding) with the reference's unmodified
 ``BK/ops/libsparse/conv.cu``, read where it lies in the reference checkout, for sm_100a
-into ``oracle/_ref/vdit_ref_libsparse.so`` (git-ignored; it travels to the GPU box with
+into ``oracle/_ref/vdit_ref_libsparse.so`` (git-ignored; it is copied to GPU machines with
 the other built libraries).  Skipped when the checkout is absent.  The reference's own
 build system (its setup.py, which also pulls in its attention and mesh sources) is not
 used.

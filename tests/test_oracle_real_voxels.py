@@ -3,7 +3,7 @@
 The reference ships three public-test samples (``fetched_info/sample_test_data/
 public_test/*/cache/vox_idxi.npz``, N = 4632..6082 in 64^3).  They are read in
 place from a reference checkout and never copied; on a machine without the
-checkout (the GPU box) these tests skip.  The reference side is its own CPU
+checkout (a GPU machine, for instance) these tests skip.  The reference side is its own CPU
 code: the lexicographic key sort of ``lib/fast_flow.py:675-679``,
 ``base_models/order.py:encode_hilbert``, ``build_order_caches_fast`` and
 ``build_conv_indices_fast`` (CPU fallbacks of ``lib/fast_kernels.py``).
