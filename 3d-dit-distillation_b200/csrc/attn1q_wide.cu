@@ -57,14 +57,17 @@ __global__ void __launch_bounds__(kFoldThreads) wide1q_fold_kernel(const __nv_bf
 // Thread t owns columns [4t, 4t + 4) of its heads' folded queries and weighted row sums.
 // Per batch of kRows rows: kRows x kHg partial scores per thread, reduced across the warp
 // by recursive halving (lane L ends with value L: row L / kHg, head L % kHg), then
-// across warps through shared memory; one thread per head updates the running max / sum
-// and turns the scores into probabilities; every thread rescales and accumulates u.
+// across warps through shared memory by warp 0, whose lanes (one per row and head) then
+// update each head's running max / sum with shuffles and turn the scores into
+// probabilities; every thread rescales and accumulates u.
 __global__ void wide1q_partial_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t n, int d, int heads,
                                       const float* __restrict__ qf, int64_t per, float* __restrict__ ws) {
     constexpr int V = kRows * kHg;                   // 32: one reduced value per lane
-    __shared__ float red[16][V];                     // up to 512 threads
-    __shared__ float sc[V];                          // scores, then probabilities
-    __shared__ float alpha[kHg], mstate[kHg], lstate[kHg];
+    // double-buffered by batch parity, so a batch needs two barriers: one before warp 0 reduces
+    // the warps' partial scores and runs the softmax, one before every thread reads the result
+    __shared__ float red[2][16][V];                  // up to 512 threads
+    __shared__ float sc[2][V];                       // probabilities
+    __shared__ float alpha[2][kHg], mstate[kHg], lstate[kHg];
     const int ngroups = (heads + kHg - 1) / kHg;
     const int rr = blockIdx.x / ngroups, hg = blockIdx.x % ngroups;
     const int nwarps = blockDim.x >> 5;
@@ -82,11 +85,6 @@ __global__ void wide1q_partial_kernel(const __nv_bfloat16* __restrict__ x, int64
             u[hl][k] = 0.f;
         }
     }
-    if (t < kHg) {
-        mstate[t] = -INFINITY;
-        lstate[t] = 0.f;
-    }
-
     // raw rows of the next batch are loaded while the current one is reduced
     uint2 nxt[kRows];
     auto fetch = [&](int64_t b) {
@@ -95,7 +93,9 @@ __global__ void wide1q_partial_kernel(const __nv_bfloat16* __restrict__ x, int64
             nxt[r] = b + r < r1 ? __ldg(reinterpret_cast<const uint2*>(x + (b + r) * ldx + col)) : make_uint2(0u, 0u);
     };
     fetch(r0);
-    for (int64_t b = r0; b < r1; b += kRows) {
+    float m_run = -INFINITY, l_run = 0.f;            // warp 0: the state of head lane % kHg
+    int par = 0;
+    for (int64_t b = r0; b < r1; b += kRows, par ^= 1) {
         float hv[kRows][4];
 #pragma unroll
         for (int r = 0; r < kRows; ++r) {
@@ -127,46 +127,45 @@ __global__ void wide1q_partial_kernel(const __nv_bfloat16* __restrict__ x, int64
                 val[i] = (up ? val[i + half] : val[i]) + recv;
             }
         }
-        red[warp][lane] = val[0];
+        red[par][warp][lane] = val[0];
         __syncthreads();
-        if (t < V) {
-            float s = 0.f;
-            for (int w = 0; w < nwarps; ++w) s += red[w][t];
-            sc[t] = (b + t / kHg < r1) ? s : -INFINITY;
-        }
-        __syncthreads();
-        if (t < kHg) {          // online softmax of head t of the group over this batch
-            const float m_old = mstate[t];
-            float mb = -INFINITY;
+        if (warp == 0) {        // lane = row * kHg + head: online softmax of the batch, per head
+            float sum = 0.f;
+            for (int w = 0; w < nwarps; ++w) sum += red[par][w][lane];
+            const int hl = lane % kHg;
+            const float sv = (b + lane / kHg < r1) ? sum : -INFINITY;
+            float mb = sv;
 #pragma unroll
-            for (int r = 0; r < kRows; ++r) mb = fmaxf(mb, sc[r * kHg + t]);
-            const float m_new = fmaxf(m_old, mb);
-            const float a = m_old == -INFINITY ? 0.f : exp2f(m_old - m_new);
-            float l = lstate[t] * a;
+            for (int o = kHg; o < 32; o <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+            const float m_new = fmaxf(m_run, mb);
+            const float a = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
+            const float pr = exp2f(sv - m_new);
+            float l = l_run * a;     // rows summed in order, as a serial loop would
 #pragma unroll
-            for (int r = 0; r < kRows; ++r) {
-                const float p = exp2f(sc[r * kHg + t] - m_new);
-                sc[r * kHg + t] = p;
-                l += p;
-            }
-            mstate[t] = m_new;
-            lstate[t] = l;
-            alpha[t] = a;
+            for (int r = 0; r < kRows; ++r) l += __shfl_sync(0xffffffffu, pr, r * kHg + hl);
+            sc[par][lane] = pr;
+            if (lane < kHg) alpha[par][lane] = a;
+            m_run = m_new;
+            l_run = l;
         }
         __syncthreads();
 #pragma unroll
         for (int hl = 0; hl < kHg; ++hl) {
-            const float a = alpha[hl];
+            const float a = alpha[par][hl];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 float acc = u[hl][k] * a;
 #pragma unroll
-                for (int r = 0; r < kRows; ++r) acc = fmaf(sc[r * kHg + hl], hv[r][k], acc);
+                for (int r = 0; r < kRows; ++r) acc = fmaf(sc[par][r * kHg + hl], hv[r][k], acc);
                 u[hl][k] = acc;
             }
         }
-        __syncthreads();        // sc and alpha are rewritten by the next batch
     }
+    if (warp == 0 && lane < kHg) {
+        mstate[lane] = m_run;
+        lstate[lane] = l_run;
+    }
+    __syncthreads();
     // partial state of this row range: per head [m, l, u[d]]
 #pragma unroll
     for (int hl = 0; hl < kHg; ++hl) {
