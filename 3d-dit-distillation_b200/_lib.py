@@ -45,6 +45,7 @@ SIGNATURES = {
     "vdit_dwconv27_plan_bytes": (ctypes.c_size_t, [_c_i64]),
     "vdit_dwconv27_plan": (ctypes.c_int, [_vp, _vp, _c_i64, _vp, ctypes.c_size_t, _vp]),
     "vdit_dwconv27_swiglu_planned": (ctypes.c_int, [_vp, _c_i64, _c_i32, _vp, _vp, _vp, _vp, _vp]),
+    "vdit_dwconv27_swiglu_planned_bf16w": (ctypes.c_int, [_vp, _c_i64, _c_i32, _vp, _vp, _vp, _vp, _vp]),
     "vdit_attention": (ctypes.c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _vp, _vp, _vp, _c_i32,
                                       _c_i32, _c_i32, _c_f32, _vp]),
     "vdit_attention_1q_workspace_bytes": (_c_sz, [_c_i32, _c_i32, _c_i64]),

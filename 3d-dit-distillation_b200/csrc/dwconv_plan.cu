@@ -320,6 +320,18 @@ __global__ void __launch_bounds__(512) dwconv_plan_kernel(const int32_t* __restr
 __device__ int g_dwplan_error = 0;
 constexpr int kErrTimeout = 3;
 
+// d.x += bf16(x.lo) * bf16(w.lo), d.y += bf16(x.hi) * bf16(w.hi): fp32 FMAs with operands read
+// straight from packed bf16 registers (fma.rn.f32.bf16: exact inputs, one rounding), which
+// saves the unpack of the features when the weights are bf16 values too
+__device__ __forceinline__ void fma_bf2(float2& d, uint32_t x, uint32_t w) {
+    asm("{.reg .b16 x0, x1, w0, w1;\n\t"
+        "mov.b32 {x0, x1}, %2;\n\t"
+        "mov.b32 {w0, w1}, %3;\n\t"
+        "fma.rn.f32.bf16 %0, x0, w0, %0;\n\t"
+        "fma.rn.f32.bf16 %1, x1, w1, %1;\n\t}"
+        : "+f"(d.x), "+f"(d.y) : "r"(x), "r"(w));
+}
+
 __device__ __forceinline__ float2 unpack_bf2(uint32_t v) {
     return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
 }
@@ -341,8 +353,10 @@ __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_
 }
 
 // Accumulates one group of 4 rows over its union taps, two taps per iteration
-// (both taps' loads issued before their FMAs).
-template <bool GLOBAL>
+// (both taps' loads issued before their FMAs).  BF16W: the weights hold bf16 values, so each
+// tap's four weights are packed to bf16 (exactly) and the FMAs take bf16 operands directly;
+// the products and sums are the same fp32 operations either way.
+template <bool GLOBAL, bool BF16W>
 __device__ __forceinline__ void accumulate_group(const Group* grp, const char* feat, const char* wb, int lane,
                                                  const __nv_bfloat16* __restrict__ hcol, int c,
                                                  float2 (&acc_a)[kGroupRows], float2 (&acc_g)[kGroupRows]) {
@@ -365,11 +379,21 @@ __device__ __forceinline__ void accumulate_group(const Group* grp, const char* f
         wv = *reinterpret_cast<const float4*>(wl + grp->taps[i] * kWRowBytes);
     };
     auto fma_tap = [&](const uint2 (&v)[kGroupRows], const float4& wv) {
-        const float2 wa = make_float2(wv.x, wv.y), wg = make_float2(wv.z, wv.w);
+        if (BF16W) {
+            __nv_bfloat162 wa2 = __floats2bfloat162_rn(wv.x, wv.y), wg2 = __floats2bfloat162_rn(wv.z, wv.w);
+            const uint32_t wa = *reinterpret_cast<uint32_t*>(&wa2), wg = *reinterpret_cast<uint32_t*>(&wg2);
 #pragma unroll
-        for (int q = 0; q < kGroupRows; ++q) {
-            acc_a[q] = tc::ffma2v(unpack_bf2(v[q].x), wa, acc_a[q]);
-            acc_g[q] = tc::ffma2v(unpack_bf2(v[q].y), wg, acc_g[q]);
+            for (int q = 0; q < kGroupRows; ++q) {
+                fma_bf2(acc_a[q], v[q].x, wa);
+                fma_bf2(acc_g[q], v[q].y, wg);
+            }
+        } else {
+            const float2 wa = make_float2(wv.x, wv.y), wg = make_float2(wv.z, wv.w);
+#pragma unroll
+            for (int q = 0; q < kGroupRows; ++q) {
+                acc_a[q] = tc::ffma2v(unpack_bf2(v[q].x), wa, acc_a[q]);
+                acc_g[q] = tc::ffma2v(unpack_bf2(v[q].y), wg, acc_g[q]);
+            }
         }
     };
     int i = 0;
@@ -391,6 +415,7 @@ __device__ __forceinline__ void accumulate_group(const Group* grp, const char* f
 
 // Warps 0..15 compute; warp 16 stages work units into a two-slot ring
 // (full: TMA bytes landed; empty: the compute warps are done with it).
+template <bool BF16W>
 __global__ void __launch_bounds__((kWarps + 1) * 32, 1) dwconv_planned_kernel(
         const __grid_constant__ CUtensorMap hmap, const __nv_bfloat16* __restrict__ h, int c,
         const void* __restrict__ plan, int64_t blocks, const float* __restrict__ w, const float* __restrict__ b,
@@ -492,9 +517,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) dwconv_planned_kernel(
                 acc_g[q] = make_float2(bias.z, bias.w);
             }
             if (overflow)
-                accumulate_group<true>(grp, feat, wb, lane, hcol, c, acc_a, acc_g);
+                accumulate_group<true, BF16W>(grp, feat, wb, lane, hcol, c, acc_a, acc_g);
             else
-                accumulate_group<false>(grp, feat, wb, lane, hcol, c, acc_a, acc_g);
+                accumulate_group<false, BF16W>(grp, feat, wb, lane, hcol, c, acc_a, acc_g);
             const int rows[kGroupRows] = {rows4.x, rows4.y, rows4.z, rows4.w};
 #pragma unroll
             for (int q = 0; q < kGroupRows; ++q) {
@@ -548,8 +573,8 @@ extern "C" int vdit_dwconv27_plan(const int32_t* idx, const int64_t* row_order, 
     return check_launch();
 }
 
-extern "C" int vdit_dwconv27_swiglu_planned(const void* h, int64_t n, int32_t c, const void* plan, const float* w,
-                                            const float* b, void* out, vdit_stream_t stream) {
+static int planned_impl(bool bf16w, const void* h, int64_t n, int32_t c, const void* plan, const float* w,
+                        const float* b, void* out, vdit_stream_t stream) {
     if (n < 0 || c <= 0 || (n > 0 && (!h || !plan || !w || !b || !out))) return VDIT_ERR_ARG;
     if (c % kTileCols) return VDIT_ERR_UNSUPPORTED;
     if (n == 0) return VDIT_OK;
@@ -567,7 +592,11 @@ extern "C" int vdit_dwconv27_swiglu_planned(const void* h, int64_t n, int32_t c,
         int sms = 0;
         e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(dwconv_planned_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+            e = cudaFuncSetAttribute(dwconv_planned_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemBytes);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(dwconv_planned_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemBytes);
         if (e != cudaSuccess) {
             record_cuda_error(e);
             return VDIT_ERR_LAUNCH;
@@ -589,8 +618,22 @@ extern "C" int vdit_dwconv27_swiglu_planned(const void* h, int64_t n, int32_t c,
     const int64_t blocks = (n + kPlanRows - 1) / kPlanRows;
     const int64_t units = blocks * (c / kTileCols);
     const int grid = (int)(units < g_sm_count[dev] ? units : g_sm_count[dev]);
-    dwconv_planned_kernel<<<grid, (kWarps + 1) * 32, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
-        m, static_cast<const __nv_bfloat16*>(h), c, plan, blocks, w, b, static_cast<__nv_bfloat16*>(out));
+    if (bf16w)
+        dwconv_planned_kernel<true><<<grid, (kWarps + 1) * 32, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
+            m, static_cast<const __nv_bfloat16*>(h), c, plan, blocks, w, b, static_cast<__nv_bfloat16*>(out));
+    else
+        dwconv_planned_kernel<false><<<grid, (kWarps + 1) * 32, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
+            m, static_cast<const __nv_bfloat16*>(h), c, plan, blocks, w, b, static_cast<__nv_bfloat16*>(out));
     count_launches(1);
     return check_launch();
+}
+
+extern "C" int vdit_dwconv27_swiglu_planned(const void* h, int64_t n, int32_t c, const void* plan, const float* w,
+                                            const float* b, void* out, vdit_stream_t stream) {
+    return planned_impl(false, h, n, c, plan, w, b, out, stream);
+}
+
+extern "C" int vdit_dwconv27_swiglu_planned_bf16w(const void* h, int64_t n, int32_t c, const void* plan,
+                                                  const float* w, const float* b, void* out, vdit_stream_t stream) {
+    return planned_impl(true, h, n, c, plan, w, b, out, stream);
 }

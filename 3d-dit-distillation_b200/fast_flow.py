@@ -143,6 +143,9 @@ class OptimizedLatDitRunner:
         self.ffn_interleaved = (2 * Fh) % 128 == 0
         self.ffn_perm = torch.arange(2 * Fh, device=self.device).view(2, Fh // 2, 2).permute(1, 0, 2).reshape(-1)
         self.blocks: List[Dict[str, torch.Tensor]] = []
+        # per block: the conv weights hold bf16 values (a bf16 model upcast), so the conv may
+        # take its bf16-operand FMAs, which give the same bits
+        self.conv_bf16w: List[bool] = []
         for b in range(a.depth):
             p = f"flow.blocks.{b}."
             w = {n: bf(p + n + ".weight") for n in ("to_qkv", "to_out", "to_out_cross", "ffn0", "ffn1")}
@@ -156,6 +159,7 @@ class OptimizedLatDitRunner:
                 w["ffn0_b"] = w["ffn0_b"][self.ffn_perm].contiguous()
                 w["conv_w"] = w["conv_w"][:, self.ffn_perm].contiguous()
                 w["conv_b"] = w["conv_b"][self.ffn_perm].contiguous()
+            self.conv_bf16w.append(fk.weights_are_bf16(w["conv_w"]))
             w["qs"], w["ks"] = f32(p + "qk_norm.q_scale"), f32(p + "qk_norm.k_scale")
             if b < cd:
                 for n in ("cond_to_qkv", "cond_to_out", "to_qkv_cross", "cond_to_qkv_cross", "cond_to_out_cross",
@@ -283,7 +287,8 @@ class OptimizedLatDitRunner:
         w = self.blocks[b]
         h2 = F.linear(h_mod, w["ffn0"], w["ffn0_b"])
         if self.ffn_interleaved:
-            y = fk.fast_sparse_conv3d_swiglu_planned(h2, w["conv_w"], w["conv_b"], geom["conv_plan"])
+            y = fk.fast_sparse_conv3d_swiglu_planned(h2, w["conv_w"], w["conv_b"], geom["conv_plan"],
+                                                     bf16_weights=self.conv_bf16w[b])
         else:
             y = fk.fast_sparse_conv3d(h2, w["conv_w"], w["conv_b"], geom["conv_indices"], fuse_swiglu=True)
         return F.linear(y, w["ffn1"], w["ffn1_b"])

@@ -268,16 +268,25 @@ def build_conv_plan(conv_indices, row_order: torch.Tensor) -> torch.Tensor:
 
 
 def fast_sparse_conv3d_swiglu_planned(feat: torch.Tensor, weight_fp32: torch.Tensor, bias_fp32: torch.Tensor,
-                                      plan: torch.Tensor) -> torch.Tensor:
+                                      plan: torch.Tensor, bf16_weights: bool = False) -> torch.Tensor:
     """silu(conv(feat)[:, C/2:]) * conv(feat)[:, :C/2] from a ``build_conv_plan``, with
     ``feat``, ``weight_fp32`` and ``bias_fp32`` in pair-interleaved column order
     (a[2k], a[2k+1], gate[2k], gate[2k+1]); bit-identical to
-    ``fast_sparse_conv3d(..., fuse_swiglu=True)`` on the de-interleaved inputs."""
+    ``fast_sparse_conv3d(..., fuse_swiglu=True)`` on the de-interleaved inputs.
+    ``bf16_weights``: the weights hold bf16 values (``weights_are_bf16``); the faster
+    bf16-operand FMAs then give the same bits."""
     n, c = feat.shape
     out = torch.empty(n, c // 2, dtype=BF16, device=feat.device)
-    check(lib().vdit_dwconv27_swiglu_planned(ptr(feat), n, c, ptr(plan), ptr(weight_fp32), ptr(bias_fp32),
-                                             ptr(out), _s(feat)), "dwconv27_swiglu_planned")
+    fn = lib().vdit_dwconv27_swiglu_planned_bf16w if bf16_weights else lib().vdit_dwconv27_swiglu_planned
+    check(fn(ptr(feat), n, c, ptr(plan), ptr(weight_fp32), ptr(bias_fp32), ptr(out), _s(feat)),
+          "dwconv27_swiglu_planned")
     return out
+
+
+def weights_are_bf16(w: torch.Tensor) -> bool:
+    """True when every value of the fp32 tensor is exactly a bf16 value (one check per
+    weight set; it selects the bf16-operand conv)."""
+    return bool((w.to(BF16).to(torch.float32) == w).all())
 
 
 def fast_sparse_conv3d(feat: torch.Tensor, weight_fp32: torch.Tensor, bias_fp32: torch.Tensor,

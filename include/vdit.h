@@ -174,6 +174,14 @@ int vdit_dwconv27_plan(const int32_t* idx, const int64_t* row_order, int64_t n, 
                        size_t plan_bytes, vdit_stream_t stream);
 int vdit_dwconv27_swiglu_planned(const void* h, int64_t n, int32_t c, const void* plan,
                                  const float* w, const float* b, void* out, vdit_stream_t stream);
+/* The same conv + SwiGLU for weights w whose every value is exactly a bf16 value (as
+ * when the reference upcasts a bf16 model's ffn_conv weight, lib/fast_flow.py:177):
+ * its FMAs read the bf16 features and the bf16-rounded weights without unpacking them,
+ * which is exact only under that precondition, and then the output is bit-identical to
+ * vdit_dwconv27_swiglu_planned.  The precondition is the caller's to check (once per
+ * weight set); the bias b has no such condition. */
+int vdit_dwconv27_swiglu_planned_bf16w(const void* h, int64_t n, int32_t c, const void* plan,
+                                       const float* w, const float* b, void* out, vdit_stream_t stream);
 
 /* ------------------------------------------------------------------ attention */
 /* Non-causal varlen flash attention on tcgen05 tensor cores (head_dim 96 or 128).

@@ -58,6 +58,8 @@ def test_shape_errors_are_reported_before_any_launch():
     assert lib.vdit_dwconv27_plan(16, 16, 5, 16, 0, None) == -5            # plan buffer too small
     assert lib.vdit_dwconv27_swiglu_planned(None, 5, 7680, None, None, None, None, None) == -1
     assert lib.vdit_dwconv27_swiglu_planned(16, 5, 960, 16, 16, 16, 16, None) == -4   # c % 128 != 0
+    assert lib.vdit_dwconv27_swiglu_planned_bf16w(None, 5, 7680, None, None, None, None, None) == -1
+    assert lib.vdit_dwconv27_swiglu_planned_bf16w(16, 5, 960, 16, 16, 16, 16, None) == -4
     with pytest.raises(RuntimeError, match="invalid argument"):
         _lib.check(-1, "probe")
 

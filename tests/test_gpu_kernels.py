@@ -290,6 +290,31 @@ def test_dwconv27_swiglu_planned(case):
     assert torch.equal(fk.fast_sparse_conv3d_swiglu_planned(hp, wp, bp, plan), ref)
 
 
+@pytest.mark.parametrize("case", ["shell", "cube", "tiny"])
+def test_dwconv27_swiglu_planned_bf16_weights(case):
+    """With bf16-valued weights (a bf16 model upcast to fp32) the bf16-operand FMAs give
+    the bits of the fp32-weight path: staged blocks (shell), blocks computed from global
+    memory (the dense cube in lexicographic order) and a single voxel."""
+    from tests.golden.make_golden import shell_voxels
+    if case == "shell":
+        vox, c = shell_voxels(16384, 64, 36.0, 0), 7680
+    elif case == "cube":
+        g = np.meshgrid(np.arange(20), np.arange(20), np.arange(20), indexing="ij")
+        vox, c = np.stack(g, -1).reshape(-1, 3).astype(np.int32), 256
+    else:
+        vox, c = np.array([[3, 4, 5]], np.int32), 256
+    h, w, b, idx, fwd = _planned_case(vox, c, 23)
+    w = w.to(torch.bfloat16).float()
+    assert fk.weights_are_bf16(w) and not fk.weights_are_bf16(w + 1e-3)
+    perm = _pair_interleave(c)
+    hp, wp, bp = h[:, perm].contiguous(), w[:, perm].contiguous(), b[perm].contiguous()
+    for order in (fwd[0], torch.arange(h.shape[0], device=DEV)):
+        plan = fk.build_conv_plan([idx], order)
+        ref = fk.fast_sparse_conv3d_swiglu_planned(hp, wp, bp, plan)
+        out = fk.fast_sparse_conv3d_swiglu_planned(hp, wp, bp, plan, bf16_weights=True)
+        assert torch.equal(out, ref), (case, (out.float() - ref.float()).abs().max().item())
+
+
 def _pair_interleave(c):
     """Column order (a[2k], a[2k+1], gate[2k], gate[2k+1]) of the staged conv's input."""
     return torch.arange(c, device=DEV).view(2, c // 4, 2).permute(1, 0, 2).reshape(-1)
