@@ -63,6 +63,34 @@ def test_one_nfe_matches_oracle(dim, hd):
     assert _lib.device_error() == 0
 
 
+def test_bf16_conv_weights_take_the_bf16_operand_conv():
+    """A model whose conv weights hold bf16 values (a bf16 checkpoint upcast, as the reference
+    does) runs the bf16-operand conv in every block, with the same bits as the fp32-weight
+    conv, in both branches."""
+    cfg = om.ModelConfig(dim=512, head_dim=128, depth=2, cond_depth=1, res=64, patch_size=256)
+    p = om.init_params(cfg, 5, weight_std=0.03, bias_std=0.02, scale_jitter=0.1)
+    keys = [k for k in p if k.endswith("ffn_conv.weight")]
+    assert len(keys) == cfg.depth
+    for k in keys:
+        p[k] = p[k].to(torch.bfloat16).float()
+    mc = {"dim": 512, "head_dim": 128, "depth": 2, "cond_depth": 1, "res": 64, "patch_size": 256,
+          "latent_scale": cfg.latent_scale}
+    runner = OptimizedLatDitRunner(LatDitModel.from_state_dict(p, mc), SolverConfig(guidance_scale=3.0),
+                                   device=torch.device(DEV))
+    assert runner.ffn_interleaved and runner.conv_bf16w == [True, True]
+    vox = shell_voxels(600, 64, 20.0, 9)
+    g = torch.Generator().manual_seed(10)
+    ctx = torch.randn(5 + 64, 512, generator=g).to(DEV, torch.bfloat16)
+    geom = runner._prepare_sample_geometry([torch.from_numpy(vox).to(DEV)], ctx)
+    xs = torch.randn(len(vox), 16, generator=g).to(DEV)
+    out = [runner.forward_flow_fast(xs, 0.5, ctx, None, geom, uncond=u) for u in (False, True)]
+    runner.conv_bf16w = [False, False]
+    ref = [runner.forward_flow_fast(xs, 0.5, ctx, None, geom, uncond=u) for u in (False, True)]
+    for a, b in zip(out, ref):
+        assert torch.equal(a, b)
+    assert _lib.device_error() == 0
+
+
 def test_sampler_matches_oracle():
     cfg, p, runner, vox, ctx_unused, _ = build(512, 128, depth=2, cdepth=1, n=700, side=8, patch=256, seed=5)
     g = torch.Generator().manual_seed(6)
