@@ -144,3 +144,16 @@ def test_arch_rejects_unbuilt_variants():
         LatDitArch.from_model_config({"io_conv": True})
     a = LatDitArch.from_model_config({"dim": 1536, "head_dim": 96})
     assert a.heads == 16
+
+
+def test_weights_are_bf16_detects_bf16_values():
+    """The check that selects the bf16-operand conv: true exactly when every fp32 value
+    is a bf16 value (a bf16 model upcast), on any device."""
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn(27, 256, generator=g)
+    assert not fk.weights_are_bf16(w)
+    wb = w.to(torch.bfloat16).float()
+    assert fk.weights_are_bf16(wb)
+    wb[3, 7] = wb[3, 7].nextafter(torch.tensor(float("inf")))   # one value off the bf16 grid
+    assert not fk.weights_are_bf16(wb)
+    assert fk.weights_are_bf16(torch.zeros(27, 8)) and fk.weights_are_bf16(torch.full((4,), -2.0 ** -130))
