@@ -56,6 +56,8 @@ SIGNATURES = {
                                          _vp]),
     "vdit_attention_1q_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_f32, _vp, _vp]),
     "vdit_dense_conv27": (ctypes.c_int, [_vp, _c_i64, _c_i32, _c_i32, _vp, _vp, _vp, _vp, _vp]),
+    "vdit_gemv": (ctypes.c_int, [_c_i32, _vp, _c_i64, _vp, _vp, _c_i64, _c_i32, _vp, _c_i64, _vp, _c_i64, _c_i32,
+                                 _c_i32, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _vp]),
     "vdit_linear": (ctypes.c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _vp, _c_i64, _c_i64, _c_i32, _c_i32, _vp]),
     "vdit_linear_qkv_rope3d": (ctypes.c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _vp, _vp, _vp, _vp, _c_i32, _vp, _vp,
                                               _vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _vp]),

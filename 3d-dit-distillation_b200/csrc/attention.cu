@@ -32,7 +32,7 @@ namespace vdit {
 
 __device__ int g_device_error = 0;
 
-namespace fmha {
+namespace attn {
 
 using namespace tc;
 
@@ -61,7 +61,7 @@ struct SegInfo {
 // tracks every earlier MMA of that thread, so "S_g(j+1) complete" also means
 // "PV_g(j) complete": the softmax group may then rescale O_g and overwrite P_g.
 template <int HD>
-__global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
+__global__ void __launch_bounds__(THREADS, 1) attention_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                               const __grid_constant__ CUtensorMap tmK,
                                                               const __grid_constant__ CUtensorMap tmV,
                                                               __nv_bfloat16* __restrict__ out, int64_t out_stride,
@@ -350,7 +350,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_fwd_kernel(const __grid_const
 }
 
 // ---------------------------------------------------------------- host side
-}  // namespace fmha
+}  // namespace attn
 
 namespace tc {
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -367,7 +367,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 }  // namespace tc
 
-namespace fmha {
+namespace attn {
 
 bool make_map(CUtensorMap* m, const void* base, int64_t rows, int heads, int hd, int64_t row_stride) {
     auto fn = tc::encode_fn();
@@ -393,18 +393,18 @@ int launch(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, __n
     static bool configured = false;
     const size_t sm = smem_bytes<HD>();
     if (!configured) {
-        const cudaError_t e = cudaFuncSetAttribute(fmha_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        const cudaError_t e = cudaFuncSetAttribute(attention_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
         if (e != cudaSuccess) {
             record_cuda_error(e);
             return VDIT_ERR_LAUNCH;
         }
         configured = true;
     }
-    fmha_fwd_kernel<HD><<<dim3(tiles, heads), THREADS, sm, s>>>(q, k, v, out, out_stride, out_rows, seg, scale_log2);
+    attention_kernel<HD><<<dim3(tiles, heads), THREADS, sm, s>>>(q, k, v, out, out_stride, out_rows, seg, scale_log2);
     return VDIT_OK;
 }
 
-}  // namespace fmha
+}  // namespace attn
 }  // namespace vdit
 
 using namespace vdit;
@@ -413,7 +413,7 @@ extern "C" int vdit_attention(const void* q, int64_t q_stride, const void* k, in
                               int64_t v_stride, void* out, int64_t out_stride, const int64_t* out_rows,
                               const int32_t* cu_q, const int32_t* cu_k, int32_t nseg, int32_t heads, int32_t hd,
                               float scale, vdit_stream_t stream) {
-    using namespace vdit::fmha;
+    using namespace vdit::attn;
     if (!q || !k || !v || !out || !cu_q || !cu_k || nseg < 1 || heads < 1) return VDIT_ERR_ARG;
     if (nseg > MAXSEG) return VDIT_ERR_UNSUPPORTED;
     if (hd != 96 && hd != 128) return VDIT_ERR_UNSUPPORTED;

@@ -115,9 +115,11 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
     const bool leader = rank == 0;
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
     volatile int* abort_flag = &sm.abort_flag;
-    const int tiles_m = (int)((m + 2 * BM - 1) / (2 * BM)), tiles_n = n / BN;
+    // a partial last column tile and a partial last k-step read zeros past n and k (the
+    // tensor maps' out-of-bounds fill), and the output store is clipped at n columns
+    const int tiles_m = (int)((m + 2 * BM - 1) / (2 * BM)), tiles_n = (n + BN - 1) / BN;
     const int ntiles = tiles_m * tiles_n;
-    const int nk = k / BK;
+    const int nk = (k + BK - 1) / BK;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -236,10 +238,13 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
                     if (ep.bias) {
 #pragma unroll
                         for (int q = 0; q < 8; ++q) {
-                            float bv[8];
-                            load8_nc(ep.bias + col0 + c * 64 + q * 8, bv);
+                            const int cb = col0 + c * 64 + q * 8;   // n is a multiple of 8
+                            if (cb < n) {
+                                float bv[8];
+                                load8_nc(ep.bias + cb, bv);
 #pragma unroll
-                            for (int j = 0; j < 8; ++j) v[q * 8 + j] += bv[j];
+                                for (int j = 0; j < 8; ++j) v[q * 8 + j] += bv[j];
+                            }
                         }
                     }
                     uint8_t* box = sm.x + (ew * 2 + (nstore & 1)) * 32 * 128;
@@ -251,7 +256,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     __syncwarp();
                     if (lane == 0) {
-                        if (row0 < m) tma_store_2d(&tmO, smem_u32(box), col0 + c * 64, row0);   // no box starts past m
+                        // no box starts past m or n (the map clips a box that crosses either)
+                        if (row0 < m && col0 + c * 64 < n) tma_store_2d(&tmO, smem_u32(box), col0 + c * 64, row0);
                         asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                     }
                 }
@@ -415,7 +421,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo, 
     if (pairs <= 0) return VDIT_ERR_LAUNCH;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = launch_config<EPI, BN>(attr, s);
-    const int64_t ntiles = ((m + 2 * BM - 1) / (2 * BM)) * (n / BN);
+    const int64_t ntiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + BN - 1) / BN);
     cfg.gridDim = dim3((unsigned)(2 * std::min<int64_t>(ntiles, pairs)));
     const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<EPI, BN>, ma, mw, mo, m, n, k, ep);
     if (e != cudaSuccess) {
@@ -427,7 +433,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo, 
 }
 
 // The pair tile width for an [m, n] output: the widest of 256, 192 and 128 columns that
-// divides n.  The mainloop is bound by shared-memory bandwidth (MMA operand reads plus TMA
+// divides n (128, with a partial last tile, when none does).  The mainloop is bound by shared-memory bandwidth (MMA operand reads plus TMA
 // fills: 128, 146 and 190 bytes per clock at the full MMA rate for those widths), so per
 // FLOP a 192-column tile runs 1.17x and a 128-column tile 1.5x the time of a 256-column
 // one, more than a narrower tile ever saves on a partial last round.
@@ -455,7 +461,7 @@ extern "C" int vdit_linear(const void* a, int64_t lda, const void* w, int64_t ld
                            int64_t ldo, int64_t m, int32_t n, int32_t k, vdit_stream_t stream) {
     using namespace vdit::gemm;
     if (!a || !w || !out || m < 0 || n <= 0 || k <= 0) return VDIT_ERR_ARG;
-    if ((n % 128 && n % 192) || k % BK) return VDIT_ERR_UNSUPPORTED;
+    if (n % 8 || k % 8) return VDIT_ERR_UNSUPPORTED;
     if (lda < k || ldw < k || ldo < n) return VDIT_ERR_ARG;
     if (!aligned16(a) || !aligned16(w) || !aligned16(out) || (bias && !aligned16(bias)) || lda % 8 || ldw % 8 ||
         ldo % 8)

@@ -6,8 +6,9 @@ Call surface of the reference's ``lib/fast_flow.py`` (``__init__``,
 ``warmup`` ``:2500-2520``, ``sample_fast`` ``:2523-3313``), exact path only.
 
 Per NFE the voxel stream x [N, D] (bf16, lexicographic voxel order) goes
-through 24 blocks.  Linears are cuBLAS GEMMs (bf16 in, fp32 accumulate);
-everything between them runs in this package's kernels: fused
+through 24 blocks.  Linears run on this package's tcgen05 GEMM (bf16 in, fp32
+accumulate in TMEM) and, for the one-row context vector of the 1-token branch
+and the time gates, on its GEMV kernel; everything between them is fused
 gate-add + LayerNorm + AdaLN, QK-RMSNorm + 3D RoPE + Hilbert gather,
 tcgen05 flash attention with the window un-permutation fused into its
 epilogue, depthwise 27-tap conv with the SwiGLU fused in, output
@@ -25,7 +26,6 @@ from pathlib import Path
 from typing import Any, Dict, List, Optional
 
 import torch
-import torch.nn.functional as F
 
 from . import fast_kernels as fk
 from .fast_sampler import SolverConfig, build_schedule
@@ -34,6 +34,15 @@ from .runtime import FlowMatchSamplingParams, LatDitConditioning
 
 BF16 = torch.bfloat16
 F32 = torch.float32
+
+# Kernel classes of the forward (the kernel timer's keys) and what bounds each: "tensor"
+# classes count FLOPs, "hbm" classes count algorithmic bytes (each tensor read or written once).
+KERNEL_CLASSES = {
+    "attention_window_self": "tensor", "attention_voxel_to_context": "tensor",
+    "attention_context_to_voxel": "tensor", "attention_context_self": "tensor",
+    "gemm_qkv_fused": "tensor", "gemm_voxel": "tensor", "gemm_context": "tensor",
+    "dwconv27_swiglu": "hbm", "gate_add_modulate": "hbm", "single_query_context_to_voxel": "hbm",
+}
 
 
 def _time_encoding(t: torch.Tensor, dim: int, max_period: float = 10000.0) -> torch.Tensor:
@@ -89,11 +98,12 @@ class OptimizedLatDitRunner:
         self._time_gates_cache: Dict[float, Dict[str, torch.Tensor]] = {}
         self._rope_2d_cache: Dict[int, tuple] = {}
         self._b0_share = None
-        # when a list, every window self-attention launch appends (start event, end event,
-        # window sizes, whether another NFE shared the GPU) to it -- the benchmark's in-step
-        # measurement of that kernel
-        self.attention_timer: Optional[list] = None
+        # when a dict, every launch of the forward's main kernels appends (start event, end
+        # event, algorithmic units, whether another NFE shared the GPU) under its kernel
+        # class (KERNEL_CLASSES): the benchmark's in-step measurement of each kernel
+        self.kernel_timer: Optional[Dict[str, list]] = None
         self._nfe_shared = False
+        self._ctx_rows = -1            # rows of the context stream in the current NFE (GEMM classes)
         # the context stream of the context blocks runs on its own CUDA stream
         self.overlap_context = True
         self._ctx_streams: Dict[int, torch.cuda.Stream] = {}
@@ -186,6 +196,10 @@ class OptimizedLatDitRunner:
                 Wox, box = f32(p + "to_out_cross.weight"), f32(p + "to_out_cross.bias")
                 w["cr1_w"], w["cr1_b"] = (Wox @ Wv).to(BF16), (Wox @ bv + box).to(BF16)
             self.blocks.append(w)
+        if a.depth > cd:
+            # the constant cross-attention maps of the plain blocks, one batched GEMV per NFE
+            self.cr1_w_all = torch.stack([self.blocks[b]["cr1_w"] for b in range(cd, a.depth)]).contiguous()
+            self.cr1_b_all = torch.stack([self.blocks[b]["cr1_b"] for b in range(cd, a.depth)]).contiguous()
         self.mean = f32("mean").reshape(1, -1)
         self.std = f32("std").reshape(1, -1)
         self._denorm_scale = (self.std * a.latent_scale).reshape(-1).contiguous()
@@ -196,6 +210,38 @@ class OptimizedLatDitRunner:
             t_seq, _, _ = build_schedule(self.solver_config)
             for t in t_seq.tolist()[:-1]:
                 self._get_time_gates(float(t))
+
+    def _run(self, kind: str, units: float, fn, *args, **kw):
+        """fn(*args, **kw); with the kernel timer on, CUDA events around it on the current
+        stream, filed under ``kind`` with its algorithmic units (FLOPs or bytes)."""
+        kt = self.kernel_timer
+        if kt is None:
+            return fn(*args, **kw)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out = fn(*args, **kw)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e1.record()
+        kt.setdefault(kind, []).append((e0, e1, float(units), self._nfe_shared))
+        return out
+
+    def _lin(self, a: torch.Tensor, w: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+        """A block linear on the tcgen05 GEMM (voxel rows or context rows)."""
+        kind = "gemm_context" if a.shape[0] == self._ctx_rows else "gemm_voxel"
+        return self._run(kind, 2.0 * a.shape[0] * a.shape[1] * w.shape[0], fk.linear, a, w, b)
+
+    def _att(self, kind: str, q, k, v, cu_q, cu_k, **kw) -> torch.Tensor:
+        """Attention launch; FLOPs 4 * sum over segments of n_q * n_k * D."""
+        units = 0.0
+        if self.kernel_timer is not None:
+            units = 4.0 * self.dim * sum((cu_q[i + 1] - cu_q[i]) * (cu_k[i + 1] - cu_k[i]) for i in range(len(cu_q) - 1))
+        return self._run(kind, units, fk.attention, q, k, v, cu_q, cu_k, self.num_heads, self.head_dim, **kw)
+
+    def _gate_add_mod(self, x, h, g, s1, sh, broadcast_h: bool = False) -> torch.Tensor:
+        """x += g * h; returns LN(x) * s1 + sh (bytes: x read and written, h read, h_mod written)."""
+        nb = x.shape[0] * x.shape[1] * 2.0 * (3 if broadcast_h else 4)
+        return self._run("gate_add_modulate", nb, fk.fast_gate_add_and_modulate, x, h, g, s1, sh,
+                         broadcast_h=broadcast_h)
 
     def _get_rope_2d_table(self, cond_size: int):
         if cond_size not in self._rope_2d_cache:
@@ -213,20 +259,21 @@ class OptimizedLatDitRunner:
             return hit
         a, D = self.arch, self.dim
         t = torch.full((1,), float(t_val) * 1000.0, dtype=F32, device=self.device)
-        h = F.silu(F.linear(_time_encoding(t, a.time_pos_features), self.W_t0, self.b_t0))
-        clf = F.silu(F.linear(h, self.W_t2, self.b_t2))[0]
-        g = F.linear(clf, self.W_g, self.b_g).view(a.depth, 9, D).clone()
+        enc = _time_encoding(t, a.time_pos_features)[0].contiguous()
+        h = fk.gemv(enc, self.W_t0, self.b_t0, out_dtype=F32, silu_out=True)
+        clf = fk.gemv(h, self.W_t2, self.b_t2, out_dtype=F32, silu_out=True)
+        g = fk.gemv(clf, self.W_g, self.b_g, out_dtype=F32).view(a.depth, 9, D).clone()
         g[:, 0::3] += 1.0
         out = {"clf": clf, "blk": g.contiguous()}
         if self.W_cg9 is not None:
-            c9 = F.linear(clf, self.W_cg9, self.b_cg9).view(a.cond_depth, 9, D).clone()
+            c9 = fk.gemv(clf, self.W_cg9, self.b_cg9, out_dtype=F32).view(a.cond_depth, 9, D).clone()
             c9[:, 0::3] += 1.0
             out["cond9"] = c9.contiguous()
         if self.W_cg2 is not None:
-            c2 = F.linear(clf, self.W_cg2, self.b_cg2).view(a.depth - a.cond_depth, 2, D).clone()
+            c2 = fk.gemv(clf, self.W_cg2, self.b_cg2, out_dtype=F32).view(a.depth - a.cond_depth, 2, D).clone()
             c2[:, 0] += 1.0
             out["cond2"] = c2.contiguous()
-        o = F.linear(clf, self.W_og, self.b_og).view(2, D).clone()
+        o = fk.gemv(clf, self.W_og, self.b_og, out_dtype=F32).view(2, D).clone()
         o[0] += 1.0
         out["out"] = o.contiguous()
         self._time_gates_cache[key] = out
@@ -265,33 +312,29 @@ class OptimizedLatDitRunner:
         D = self.dim
         fwd, bwd, cu, _ = geom["order_caches"][b % len(geom["order_caches"])]
         if self.fused_qkv:
-            qkv_s = fk.linear_qkv_rope3d(h_mod, w["to_qkv"], w["to_qkv_b"], w["qs"], w["ks"], self.cos3, self.sin3,
-                                         geom["h_coords"], bwd, H, HD)
+            qkv_s = self._run("gemm_qkv_fused", 2.0 * h_mod.shape[0] * D * 3 * D, fk.linear_qkv_rope3d, h_mod,
+                              w["to_qkv"], w["to_qkv_b"], w["qs"], w["ks"], self.cos3, self.sin3, geom["h_coords"],
+                              bwd, H, HD)
         else:
-            qkv = F.linear(h_mod, w["to_qkv"], w["to_qkv_b"])
+            qkv = self._lin(h_mod, w["to_qkv"], w["to_qkv_b"])
             qkv_s = fk.fused_qknorm_rope3d_gather(qkv, w["qs"], w["ks"], self.cos3, self.sin3, geom["h_coords"], fwd,
                                                   H, HD)
-        timer = self.attention_timer
-        if timer is not None:
-            e0 = torch.cuda.Event(enable_timing=True)
-            e0.record()
-        o = fk.attention(qkv_s[:, :D], qkv_s[:, D:2 * D], qkv_s[:, 2 * D:], cu.host, cu.host, H, HD, out_rows=fwd)
-        if timer is not None:
-            e1 = torch.cuda.Event(enable_timing=True)
-            e1.record()
-            timer.append((e0, e1, [cu.host[i + 1] - cu.host[i] for i in range(len(cu.host) - 1)],
-                          self._nfe_shared))
-        return F.linear(o, w["to_out"], w["to_out_b"])
+        o = self._att("attention_window_self", qkv_s[:, :D], qkv_s[:, D:2 * D], qkv_s[:, 2 * D:], cu.host, cu.host,
+                      out_rows=fwd)
+        return self._lin(o, w["to_out"], w["to_out_b"])
 
     def _ffn(self, b: int, h_mod: torch.Tensor, geom) -> torch.Tensor:
         w = self.blocks[b]
-        h2 = F.linear(h_mod, w["ffn0"], w["ffn0_b"])
+        h2 = self._lin(h_mod, w["ffn0"], w["ffn0_b"])
+        n, f2 = h2.shape
+        conv_bytes = n * f2 * 2.0 + n * (f2 // 2) * 2.0 + 27 * f2 * 4.0 + n * 27 * 4.0
         if self.ffn_interleaved:
-            y = fk.fast_sparse_conv3d_swiglu_planned(h2, w["conv_w"], w["conv_b"], geom["conv_plan"],
-                                                     bf16_weights=self.conv_bf16w[b])
+            y = self._run("dwconv27_swiglu", conv_bytes, fk.fast_sparse_conv3d_swiglu_planned, h2, w["conv_w"],
+                          w["conv_b"], geom["conv_plan"], bf16_weights=self.conv_bf16w[b])
         else:
-            y = fk.fast_sparse_conv3d(h2, w["conv_w"], w["conv_b"], geom["conv_indices"], fuse_swiglu=True)
-        return F.linear(y, w["ffn1"], w["ffn1_b"])
+            y = self._run("dwconv27_swiglu", conv_bytes, fk.fast_sparse_conv3d, h2, w["conv_w"], w["conv_b"],
+                          geom["conv_indices"], fuse_swiglu=True)
+        return self._lin(y, w["ffn1"], w["ffn1_b"])
 
     @torch.no_grad()
     def forward_flow_fast(self, xt_sorted: torch.Tensor, t_val: float, context: torch.Tensor,
@@ -308,6 +351,7 @@ class OptimizedLatDitRunner:
         N = xt_sorted.shape[0]
         c = (torch.zeros_like(context) if uncond else context).reshape(-1, D).to(BF16).contiguous().clone()
         L = c.shape[0]
+        self._ctx_rows = L if L != N else -1
         cos2, sin2 = geom["cos_cond_2d"], geom["sin_cond_2d"]
         x = fk.patchify(xt_sorted, self.W_patch)
         h_mod = fk.fast_modulate(x, None, G[0, 0], G[0, 1])
@@ -328,56 +372,59 @@ class OptimizedLatDitRunner:
             if b < cd:
                 CG = CG9[b]
                 with torch.cuda.stream(side):
-                    qkvc = F.linear(c_mod, w["cond_to_qkv"], w["cond_to_qkv_b"])
+                    qkvc = self._lin(c_mod, w["cond_to_qkv"], w["cond_to_qkv_b"])
                     fk.fused_qknorm_rope2d_cond_inplace(qkvc, w["cqs"], w["cks"], cos2, sin2, H, HD, n_prefix=5)
-                    oc = fk.flash_cond_self_attn(qkvc, H, HD)
-                    hc = F.linear(oc, w["cond_to_out"], w["cond_to_out_b"])
-                    c_mod = fk.fast_gate_add_and_modulate(c, hc, CG[2], CG[3], CG[4])
-                    qkvcc = F.linear(c_mod, w["cond_to_qkv_cross"], w["cond_to_qkv_cross_b"])
+                    oc = self._att("attention_context_self", qkvc[:, :D], qkvc[:, D:2 * D], qkvc[:, 2 * D:],
+                                   [0, L], [0, L])
+                    hc = self._lin(oc, w["cond_to_out"], w["cond_to_out_b"])
+                    c_mod = self._gate_add_mod(c, hc, CG[2], CG[3], CG[4])
+                    qkvcc = self._lin(c_mod, w["cond_to_qkv_cross"], w["cond_to_qkv_cross_b"])
             h = self._self_attention(b, h_mod, geom)
-            h_mod = fk.fast_gate_add_and_modulate(x, h, G[b, 2], G[b, 3], G[b, 4])
+            h_mod = self._gate_add_mod(x, h, G[b, 2], G[b, 3], G[b, 4])
             if b == 0 and share:
                 x0 = x.clone()
                 ev0 = torch.cuda.Event()
                 ev0.record()
                 self._b0_share = (round(float(t_val), 7), x0, ev0)
             if b < cd:
-                qkvx = F.linear(h_mod, w["to_qkv_cross"], w["to_qkv_cross_b"])
+                qkvx = self._lin(h_mod, w["to_qkv_cross"], w["to_qkv_cross_b"])
                 if side is not main:
                     main.wait_stream(side)                 # qkvcc is ready
                     qkvcc.record_stream(main)
                     side.wait_stream(main)                 # qkvx is ready
                     qkvx.record_stream(side)
                 with torch.cuda.stream(side):
-                    ocx = fk.attention(qkvcc[:, :D], qkvx[:, D:2 * D], qkvx[:, 2 * D:], [0, L], [0, N], H, HD)
-                    hcx = F.linear(ocx, w["cond_to_out_cross"], w["cond_to_out_cross_b"])
-                    c_mod = fk.fast_gate_add_and_modulate(c, hcx, CG[5], CG[6], CG[7])
-                    hc2 = F.linear(c_mod, w["cond_ffn0"], w["cond_ffn0_b"])
-                    hcf = F.linear(fk.fast_swiglu_from_packed(hc2), w["cond_ffn1"], w["cond_ffn1_b"])
+                    ocx = self._att("attention_context_to_voxel", qkvcc[:, :D], qkvx[:, D:2 * D], qkvx[:, 2 * D:],
+                                    [0, L], [0, N])
+                    hcx = self._lin(ocx, w["cond_to_out_cross"], w["cond_to_out_cross_b"])
+                    c_mod = self._gate_add_mod(c, hcx, CG[5], CG[6], CG[7])
+                    hc2 = self._lin(c_mod, w["cond_ffn0"], w["cond_ffn0_b"])
+                    hcf = self._lin(fk.fast_swiglu_from_packed(hc2), w["cond_ffn1"], w["cond_ffn1_b"])
                     if b + 1 < cd:
-                        c_mod = fk.fast_gate_add_and_modulate(c, hcf, CG[8], CG9[b + 1, 0], CG9[b + 1, 1])
+                        c_mod = self._gate_add_mod(c, hcf, CG[8], CG9[b + 1, 0], CG9[b + 1, 1])
                     else:
                         fk.fast_gate_add(c, hcf, CG[8])
                     if b + 1 == cd:
                         # the context is frozen from here on: the K/V of every remaining block
                         kv_frozen = self._frozen_context_kv(c, CG2)
-                ox = fk.attention(qkvx[:, :D], qkvcc[:, D:2 * D], qkvcc[:, 2 * D:], [0, N], [0, L], H, HD)
-                hx = F.linear(ox, w["to_out_cross"], w["to_out_cross_b"])
-                h_mod = fk.fast_gate_add_and_modulate(x, hx, G[b, 5], G[b, 6], G[b, 7])
+                ox = self._att("attention_voxel_to_context", qkvx[:, :D], qkvcc[:, D:2 * D], qkvcc[:, 2 * D:], [0, N],
+                               [0, L])
+                hx = self._lin(ox, w["to_out_cross"], w["to_out_cross_b"])
+                h_mod = self._gate_add_mod(x, hx, G[b, 5], G[b, 6], G[b, 7])
             else:
                 if cd == 0 and b == 0:
                     kv_frozen = self._frozen_context_kv(c, CG2)
-                q = F.linear(h_mod, w["to_q_cross"], w["to_q_cross_b"])
+                q = self._lin(h_mod, w["to_q_cross"], w["to_q_cross_b"])
                 kv, ready = kv_frozen[b - cd]
                 if side is not main:
                     main.wait_event(ready)
                     kv.record_stream(main)
-                ox = fk.attention(q, kv[:, :D], kv[:, D:], [0, N], [0, L], H, HD)
-                hx = F.linear(ox, w["to_out_cross"], w["to_out_cross_b"])
-                h_mod = fk.fast_gate_add_and_modulate(x, hx, G[b, 5], G[b, 6], G[b, 7])
+                ox = self._att("attention_voxel_to_context", q, kv[:, :D], kv[:, D:], [0, N], [0, L])
+                hx = self._lin(ox, w["to_out_cross"], w["to_out_cross_b"])
+                h_mod = self._gate_add_mod(x, hx, G[b, 5], G[b, 6], G[b, 7])
             hf = self._ffn(b, h_mod, geom)
             if b + 1 < self.depth:
-                h_mod = fk.fast_gate_add_and_modulate(x, hf, G[b, 8], G[b + 1, 0], G[b + 1, 1])
+                h_mod = self._gate_add_mod(x, hf, G[b, 8], G[b + 1, 0], G[b + 1, 1])
             else:
                 fk.fast_gate_add(x, hf, G[b, 8])
         if side is not main:
@@ -392,7 +439,7 @@ class OptimizedLatDitRunner:
             C2 = CG2[b - self.cond_depth]
             w = self.blocks[b]
             cm = fk.fast_modulate(c, None, C2[0], C2[1])
-            kv = F.linear(cm, w["cond_to_kv_cross"], w["cond_to_kv_cross_b"])
+            kv = self._lin(cm, w["cond_to_kv_cross"], w["cond_to_kv_cross_b"])
             ev = torch.cuda.Event()
             ev.record()
             out.append((kv, ev))
@@ -428,8 +475,8 @@ class OptimizedLatDitRunner:
             c.record_stream(side)
 
         def mod_lin(scale1, shift, wk, bk, blk):
-            """bf16 Linear(LN(c) * scale1 + shift) of the context vector."""
-            return F.linear(fk.vec_ln_modulate(c, scale1, shift), blk[wk], blk[bk])
+            """bf16 Linear(LN(c) * scale1 + shift) of the context vector (one GEMV launch)."""
+            return fk.gemv(c, blk[wk], blk[bk], x_mode=fk.GEMV_X_LN_MOD, mod_scale=scale1, mod_shift=shift)
 
         def on_side_event():
             ev = torch.cuda.Event()
@@ -461,13 +508,14 @@ class OptimizedLatDitRunner:
                 # the context vector is frozen from here on: the constant cross-attention output
                 # of every remaining block, one event each
                 with torch.cuda.stream(side):
-                    for bb in range(cd, self.depth):
-                        C2 = CG2[bb - cd]
-                        xc = mod_lin(C2[0], C2[1], "cr1_w", "cr1_b", self.blocks[bb])
-                        consts.append((xc, on_side_event()))
+                    # one batched GEMV: block bb's map of LN(c) * (1 + cs_bb) + csh_bb
+                    xc_all = fk.gemv(c, self.cr1_w_all, self.cr1_b_all, x_mode=fk.GEMV_X_LN_MOD,
+                                     mod_scale=CG2[:, 0], mod_shift=CG2[:, 1])
+                    ev = on_side_event()
+                    consts = [(xc_all[i], ev) for i in range(self.depth - cd)]
             h = self._self_attention(b, h_mod, geom) if b >= start else None
             if h is not None and b < cd:
-                h_mod = fk.fast_gate_add_and_modulate(x, h, G[b, 2], G[b, 3], G[b, 4])
+                h_mod = self._gate_add_mod(x, h, G[b, 2], G[b, 3], G[b, 4])
             if b < cd:
                 # the context query attends over K/V = cross linear of the modulated stream;
                 # attention_1q_wide reads the stream itself (K/V are never formed)
@@ -477,16 +525,18 @@ class OptimizedLatDitRunner:
                     kv_ready.record(main)
                     main.wait_event(q_ready)
                     qo.record_stream(main)
-                h_mod = fk.fast_gate_add_and_modulate(x, x_const, G[b, 5], G[b, 6], G[b, 7], broadcast_h=True)
+                h_mod = self._gate_add_mod(x, x_const, G[b, 5], G[b, 6], G[b, 7], broadcast_h=True)
                 with torch.cuda.stream(side):
                     if two:
                         side.wait_event(kv_ready)
                         h_kv.record_stream(side)
-                    o1 = fk.attention_1q_wide(q_cc, h_kv, w["kvx_w"], w["kvx_b"], H, HD)   # bf16 [D]
-                    fk.vec_gate_residual_(c, F.linear(o1, w["cond_to_out_cross"], w["cond_to_out_cross_b"]), CG[5])
+                    o1 = self._run("single_query_context_to_voxel", h_kv.numel() * 2.0 + w["kvx_w"].numel() * 2.0,
+                                   fk.attention_1q_wide, q_cc, h_kv, w["kvx_w"], w["kvx_b"], H, HD)   # bf16 [D]
+                    fk.vec_gate_residual_(c, fk.gemv(o1, w["cond_to_out_cross"], w["cond_to_out_cross_b"]), CG[5])
                     a_g = mod_lin(CG[6], CG[7], "cond_ffn0", "cond_ffn0_b", w)    # bf16 [2F]
-                    y = fk.fast_swiglu_from_packed(a_g.view(1, -1))                 # silu(g) * a, bf16
-                    fk.vec_gate_residual_(c, F.linear(y, w["cond_ffn1"], w["cond_ffn1_b"]), CG[8])
+                    # cond_ffn1(silu(g) * a): the SwiGLU of the packed vector runs in the GEMV prologue
+                    fk.vec_gate_residual_(c, fk.gemv(a_g, w["cond_ffn1"], w["cond_ffn1_b"], x_mode=fk.GEMV_X_SWIGLU),
+                                          CG[8])
             else:
                 x_const, ready = consts[b - cd]
                 if two:
@@ -495,12 +545,13 @@ class OptimizedLatDitRunner:
                 if h is not None:
                     # the self-attention and the constant cross-attention gate-adds in one pass
                     # (the modulation between them feeds nothing in this branch)
-                    h_mod = fk.fast_gate_add2_and_modulate(x, h, G[b, 2], x_const, G[b, 5], G[b, 6], G[b, 7])
+                    h_mod = self._run("gate_add_modulate", x.numel() * 8.0, fk.fast_gate_add2_and_modulate, x, h,
+                                      G[b, 2], x_const, G[b, 5], G[b, 6], G[b, 7])
                 else:
-                    h_mod = fk.fast_gate_add_and_modulate(x, x_const, G[b, 5], G[b, 6], G[b, 7], broadcast_h=True)
+                    h_mod = self._gate_add_mod(x, x_const, G[b, 5], G[b, 6], G[b, 7], broadcast_h=True)
             hf = self._ffn(b, h_mod, geom)
             if b + 1 < self.depth:
-                h_mod = fk.fast_gate_add_and_modulate(x, hf, G[b, 8], G[b + 1, 0], G[b + 1, 1])
+                h_mod = self._gate_add_mod(x, hf, G[b, 8], G[b + 1, 0], G[b + 1, 1])
             else:
                 fk.fast_gate_add(x, hf, G[b, 8])
         if two:
@@ -512,7 +563,7 @@ class OptimizedLatDitRunner:
     def encode_context(self, dino_features: torch.Tensor) -> torch.Tensor:
         """image_map: [1, L, 1280] -> [L, D] bf16 (``core.py:87-97``)."""
         d = dino_features.to(self.device, BF16).reshape(-1, dino_features.shape[-1])
-        return F.linear(d, self.W_image, self.b_image)
+        return fk.linear(d, self.W_image, self.b_image)
 
     @torch.no_grad()
     def sample_fast(self, vox_idxs: List[torch.Tensor], conditioning: LatDitConditioning, *,

@@ -319,7 +319,7 @@ def dense_sparse_conv3d(feat: torch.Tensor, weight_t_bf16: torch.Tensor, bias_fp
 def linear(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
            out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``F.linear(a, w, bias)`` for bf16 2D ``a`` [M, K] (row stride free) and a
-    contiguous bf16 weight [N, K] on the tcgen05 GEMM (N a multiple of 128 or 192, K % 64 == 0)."""
+    contiguous bf16 weight [N, K] on the tcgen05 GEMM (N and K multiples of 8)."""
     if a.dtype != BF16 or w.dtype != BF16 or a.dim() != 2 or w.dim() != 2 or a.shape[1] != w.shape[1]:
         raise ValueError(f"linear: a {tuple(a.shape)} {a.dtype} and w {tuple(w.shape)} {w.dtype} "
                          "must be 2D bf16 with the same K")
@@ -336,6 +336,54 @@ def linear(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None
     check(lib().vdit_linear(ptr(a), a.stride(0), ptr(w), w.stride(0), ptr(bias), ptr(out), out.stride(0), m, n, k,
                             _s(a)), "linear")
     return out
+
+
+GEMV_X_BF16, GEMV_X_F32, GEMV_X_LN_MOD, GEMV_X_SWIGLU = 0, 1, 2, 3
+
+
+def gemv(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None, *, x_mode: Optional[int] = None,
+         mod_scale: Optional[torch.Tensor] = None, mod_shift: Optional[torch.Tensor] = None,
+         out_dtype: torch.dtype = BF16, silu_out: bool = False) -> torch.Tensor:
+    """One-row linear(s) ``act(W x' + b)`` on the GEMV kernel.  ``w`` is [n, k] or a batch
+    [B, n, k] (bf16 or fp32, contiguous), ``bias`` [n] / [B, n] of ``w``'s dtype.  ``x'`` is
+    formed from ``x`` by the prologue ``x_mode`` (default: the plain vector of ``x``'s dtype):
+    ``GEMV_X_LN_MOD`` = bf16(LN(x) * mod_scale + mod_shift) of an fp32 [k] vector (per-batch
+    ``mod_scale``/``mod_shift`` as [B, k] views), ``GEMV_X_SWIGLU`` = bf16(silu(g) * a) of a
+    bf16 [2k] vector [a | g].  Returns [n] or [B, n] in ``out_dtype`` (bf16 or fp32)."""
+    batched = w.dim() == 3
+    wb = w if batched else w.unsqueeze(0)
+    B, n, k = wb.shape
+    if w.dtype not in (BF16, torch.float32) or not wb.is_contiguous():
+        raise ValueError("gemv: w must be contiguous bf16 or fp32 [n, k] or [B, n, k]")
+    if bias is not None and (bias.dtype != w.dtype or bias.numel() != B * n or not bias.is_contiguous()):
+        raise ValueError(f"gemv: bias must be contiguous {w.dtype} with {B * n} elements")
+    if x_mode is None:
+        x_mode = GEMV_X_F32 if x.dtype == torch.float32 else GEMV_X_BF16
+    want = {GEMV_X_BF16: (BF16, k), GEMV_X_F32: (torch.float32, k), GEMV_X_LN_MOD: (torch.float32, k),
+            GEMV_X_SWIGLU: (BF16, 2 * k)}[x_mode]
+    if x.dtype != want[0] or x.stride(-1) != 1 or x.shape[-1] != want[1]:
+        raise ValueError(f"gemv: x must be {want[0]} with {want[1]} elements per vector (mode {x_mode})")
+    x_bs = x.stride(0) if x.dim() == 2 else 0
+    if x.dim() == 2 and x.shape[0] != B:
+        raise ValueError("gemv: a batch of inputs needs one vector per weight matrix")
+    mod_bs = 0
+    if x_mode == GEMV_X_LN_MOD:
+        if mod_scale is None or mod_shift is None:
+            raise ValueError("gemv: GEMV_X_LN_MOD needs mod_scale and mod_shift")
+        for t in (mod_scale, mod_shift):
+            if t.dtype != torch.float32 or t.stride(-1) != 1 or t.shape[-1] != k:
+                raise ValueError("gemv: mod_scale / mod_shift must be fp32 with unit stride and k columns")
+        if mod_scale.dim() == 2:
+            if mod_scale.shape[0] != B or mod_scale.stride(0) != mod_shift.stride(0):
+                raise ValueError("gemv: per-batch mod_scale / mod_shift need one row per entry and one stride")
+            mod_bs = mod_scale.stride(0)
+    if out_dtype not in (BF16, torch.float32):
+        raise ValueError("gemv: out_dtype must be bf16 or fp32")
+    out = torch.empty(B, n, dtype=out_dtype, device=w.device)
+    check(lib().vdit_gemv(x_mode, ptr(x), x_bs, ptr(mod_scale), ptr(mod_shift), mod_bs, int(w.dtype == torch.float32),
+                          ptr(wb), n * k, ptr(bias), n, int(out_dtype == torch.float32), int(silu_out), ptr(out), n,
+                          n, k, B, _s(w)), "gemv")
+    return out if batched else out[0]
 
 
 def linear_qkv_rope3d(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, q_scale: torch.Tensor,

@@ -376,7 +376,8 @@ def gemm_bench(w, reps: int = 20):
     shapes = [("to_qkv", w.n, D, 3 * D), ("to_out", w.n, D, D), ("ffn0", w.n, D, F2),
               ("ffn1", w.n, F2 // 2, D), ("cond_to_qkv", w.ctx_tokens, D, 3 * D),
               ("cond_to_out", w.ctx_tokens, D, D), ("cond_to_kv_cross", w.ctx_tokens, D, 2 * D),
-              ("cond_ffn0", w.ctx_tokens, D, F2), ("cond_ffn1", w.ctx_tokens, F2 // 2, D)]
+              ("cond_ffn0", w.ctx_tokens, D, F2), ("cond_ffn1", w.ctx_tokens, F2 // 2, D),
+              ("image_map", w.ctx_tokens, w.arch.dino_dim, D)]
     g = torch.Generator(device="cuda").manual_seed(9)
     s = torch.cuda.current_stream()
     res = []
@@ -559,11 +560,13 @@ def graph_bench(w, reps: int = 5):
     return out
 
 
-def c5_bench(args, rank: int, ws: int, dev, dist):
-    """The sharded batch: ``--samples`` C5 samples (N=32768 ellipsoid-union voxels in 128^3,
+def c5_bench(rank: int, ws: int, dev, dist, samples: int = 0, steps: int = 1, warmup: int = 1,
+             model=None) -> dict:
+    """The sharded batch: ``samples`` C5 samples (N=32768 ellipsoid-union voxels in 128^3,
     default 16) split round-robin over the ranks, latents gathered to rank 0 over NCCL.
     One step processes the whole batch once (strong scaling: the batch is fixed, the
-    ranks share it); device time from CUDA events, max over ranks."""
+    ranks share it); device time from CUDA events, max over ranks, with each rank's own
+    time and the gather's share.  ``model`` (a LatDitModel on ``dev``) reuses its weights."""
     from vdit import _lib
     from vdit import distributed as vd
     from vdit.fast_sampler import SolverConfig
@@ -571,54 +574,106 @@ def c5_bench(args, rank: int, ws: int, dev, dist):
     from vdit.solution import Solution
     from vdit.workloads import C5
     w = C5()
-    samples = args.samples or w.samples
+    samples = samples or w.samples
     if samples % ws:
-        raise SystemExit(f"--samples {samples} does not split evenly over {ws} ranks")
-    model = LatDitModel.random(w.arch, seed=0, device=dev)
+        raise SystemExit(f"{samples} C5 samples do not split evenly over {ws} ranks")
+    model = LatDitModel(w.arch, model.state) if model is not None else LatDitModel.random(w.arch, seed=0, device=dev)
     solver = SolverConfig(num_inference_steps=4, n_guided_steps=3, n_unguided_steps=1, guidance_scale=w.guidance)
     runner = Solution(model, solver_config=solver, device=dev).runner
     inps = [w.inputs(seed=500 + i, device=dev) for i in range(rank, samples, ws)]
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    s = torch.cuda.current_stream()
+    gather_evs = []
 
-    def step():
+    def step(timed_gather=False):
         lats = [runner.sample_with_context(i["vox"], i["context"], noise=i["noise"]) for i in inps]
         if dist is not None:
+            if timed_gather:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
             vd.gather_latents(lats, rank, ws)
+            if timed_gather:
+                e1.record(s)
+                gather_evs.append((e0, e1))
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
-    s = torch.cuda.current_stream()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     launches0 = _lib.launch_count()
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(torch.cuda.current_device()) as clk:
-        for i in range(args.steps):
+        for i in range(steps):
             _l2_flush(flush)
             evs[i][0].record(s)
-            step()
+            step(timed_gather=True)
             evs[i][1].record(s)
         torch.cuda.synchronize()
-    launches = (_lib.launch_count() - launches0) // max(args.steps, 1)
-    t = torch.tensor([sum(a.elapsed_time(b) for a, b in evs) / args.steps], device=dev)
+    launches = (_lib.launch_count() - launches0) // max(steps, 1)
+    mine = sum(a.elapsed_time(b) for a, b in evs) / steps
+    gather_ms = sum(a.elapsed_time(b) for a, b in gather_evs) / steps if gather_evs else 0.0
+    per_rank = torch.tensor([mine, gather_ms], device=dev)
     if dist is not None:
+        allr = [torch.zeros_like(per_rank) for _ in range(ws)]
         dist.barrier()
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_step = float(t.item())
+        dist.all_gather(allr, per_rank)
+        allr = torch.stack(allr).cpu()
+    else:
+        allr = per_rank.cpu()[None]
+    ms_step = float(allr[:, 0].max())
     assert _lib.device_error() == 0, "device error word set during the benchmark"
-    if rank == 0:
-        print(json.dumps({
-            "metric": METRIC, "value": samples * NFE_PER_SAMPLE * w.n / (ms_step / 1e3), "unit": UNIT,
-            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "strong", "samples_per_s": samples / (ms_step / 1e3),
-            "ms_per_sample_per_gpu": ms_step * ws / samples, "dtype": "bf16",
-            "data": "synthetic (seeded ellipsoid-union voxels, N(0,1) context, random-init weights)",
-            "config": {"workload": f"C5 sharded batch: {samples} samples x N={w.n} (1-3 ellipsoid shells in "
-                                   f"{w.grid}^3), 24-block DiT, 4101x1536 context, 4-step exact solver = 7 NFE each",
-                       "global_batch": samples, "seq_len": w.n, "parallelism": f"samples x{ws}",
-                       "l2": "256 MiB L2 flush before every timed step"},
-            "gpu_launches": int(launches), "clocks": clk.summary()}), flush=True)
+    del runner
+    return {
+        "metric": METRIC, "value": samples * NFE_PER_SAMPLE * w.n / (ms_step / 1e3), "unit": UNIT,
+        "samples_per_s": samples / (ms_step / 1e3), "ms_per_step": ms_step, "steps": steps, "warmup": warmup,
+        "ms_per_sample": ms_step * ws / samples, "scaling": "strong",
+        "rank_ms_min": float(allr[:, 0].min()), "rank_ms_max": ms_step,
+        "gather_ms_max": float(allr[:, 1].max()),
+        "config": {"workload": f"C5 sharded batch: {samples} samples x N={w.n} (1-3 ellipsoid shells in "
+                               f"{w.grid}^3), 24-block DiT, 4101x1536 context, 4-step exact solver = 7 NFE each",
+                   "global_batch": samples, "seq_len": w.n, "parallelism": f"samples x{ws}",
+                   "l2": "256 MiB L2 flush before every timed step"},
+        "gpu_launches": int(launches), "clocks": clk.summary()}
+
+
+def kernel_table(timer: dict, hbm_peak: float, tensor_peak: float, peak_kind: str) -> list:
+    """Per kernel class: launches, average CUDA-event duration, algorithmic FLOPs or bytes
+    per launch and the fraction of the measured peak (sustained bf16 GEMM rate for
+    tensor-core classes, HBM copy bandwidth for byte-bound ones)."""
+    from vdit.fast_flow import KERNEL_CLASSES
+    rows = []
+    for kind, ev in timer.items():
+        if not ev:
+            continue
+        ms = statistics.fmean(a.elapsed_time(b) for a, b, _, _ in ev)
+        units = statistics.fmean(u for _, _, u, _ in ev)
+        bound = KERNEL_CLASSES.get(kind, "tensor")
+        if bound == "tensor":
+            ach, unit, peak = units / (ms / 1e3) / 1e12, "TFLOP/s", tensor_peak
+        else:
+            ach, unit, peak = units / (ms / 1e3) / 1e9, "GB/s", hbm_peak
+        rows.append({"kernel": kind, "bound": bound, "launches": len(ev), "ms_per_launch": ms,
+                     "units_per_launch": units, "achieved": ach, "unit": unit, "peak": peak, "frac": ach / peak,
+                     "total_ms": ms * len(ev),
+                     "peak_kind": f"{peak_kind} {'sustained bf16' if bound == 'tensor' else 'HBM copy'}"})
+    rows.sort(key=lambda r: -r["total_ms"])
+    return rows
+
+
+def attention_traffic():
+    """DRAM bytes per launch of the window self-attention kernel from the committed ncu
+    capture, when it was taken on the current kernel source (its SHA-256 is recorded with
+    it); None otherwise."""
+    import hashlib
+    tp = ROOT / "profiles" / "attention_traffic.json"
+    if not tp.exists():
+        return None
+    d = json.loads(tp.read_text())
+    src = ROOT / "3d-dit-distillation_b200" / "csrc" / "attention.cu"
+    if d.get("source_sha256") != hashlib.sha256(src.read_bytes()).hexdigest():
+        return None
+    return d.get("dram_bytes_per_launch")
 
 
 def main():
@@ -634,6 +689,8 @@ def main():
                                        "c5", "hbm"], default=None,
                     help="run only one kernel on the workload's shapes (small ncu case); c5: the sharded batch")
     ap.add_argument("--samples", type=int, default=0, help="--only c5: batch size (default 16)")
+    ap.add_argument("--c5-steps", type=int, default=1, help="timed passes of the C5 batch in the default run")
+    ap.add_argument("--no-c5", action="store_true", help="skip the C5 sharded batch in the default run")
     ap.add_argument("--reps", type=int, default=10, help="--only hbm: timed launches per kernel")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -655,13 +712,17 @@ def main():
     torch.cuda.set_device(dev)
     w = C4()
     if args.only == "c5":
-        c5_bench(args, rank, ws, dev, dist)
+        r = c5_bench(rank, ws, dev, dist, samples=args.samples, steps=args.steps, warmup=args.warmup)
+        if rank == 0:
+            print(json.dumps(dict(r, n_gpus=ws, higher_is_better=True, dtype="bf16",
+                                  data="synthetic (seeded ellipsoid-union voxels, N(0,1) context, random-init "
+                                       "weights)")), flush=True)
         if dist is not None:
             dist.destroy_process_group()
         return
     if args.only == "attention":
         flops, ms = attention_roofline(w, None)
-        print(json.dumps({"kernel": "fmha_fwd_kernel<128>", "ms_per_launch": ms, "tflops": flops / ms / 1e9}))
+        print(json.dumps({"kernel": "attention_kernel<128>", "ms_per_launch": ms, "tflops": flops / ms / 1e9}))
         return
     if args.only == "qknorm":
         print(json.dumps(qknorm_bench(w)))
@@ -727,8 +788,8 @@ def main():
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
-    att_events: list = []
-    runner.attention_timer = att_events          # window self-attention launches inside the timed steps
+    ktimer: dict = {}
+    runner.kernel_timer = ktimer                 # the main kernels' launches inside the timed steps
     with ClockSampler(local) as clk:
         for i in range(args.steps):
             _l2_flush(flush)
@@ -736,7 +797,7 @@ def main():
             step()
             evs[i][1].record(s)
         torch.cuda.synchronize()
-    runner.attention_timer = None
+    runner.kernel_timer = None
     launches = (_lib.launch_count() - launches0) // max(args.steps, 1)
     total_ms = sum(a.elapsed_time(b) for a, b in evs)
     t = torch.tensor([total_ms], device=dev)
@@ -797,19 +858,25 @@ def main():
     tflops_sustained = _peaks_sustained()
     # live: average duration of the window self-attention launches inside the timed steps
     # (CUDA events on their stream), against the sustained GEMM peak
+    att_events = ktimer["attention_window_self"]
     live_ms = statistics.fmean(a.elapsed_time(b) for a, b, _, _ in att_events)
-    flops = statistics.fmean(sum(4.0 * n * n * w.arch.dim for n in sizes) for _, _, sizes, _ in att_events)
+    flops = statistics.fmean(u for _, _, u, _ in att_events)
     achieved = flops / (live_ms / 1e3) / 1e12
     # the same launches restricted to steps where only one NFE runs (the unguided step):
     # in guided steps the conditional and the 1-token NFE run on two streams and share the GPU
-    solo = [(a, b, sz) for a, b, sz, shared in att_events if not shared]
-    solo_ms = statistics.fmean(a.elapsed_time(b) for a, b, _ in solo) if solo else None
+    solo = [(a, b) for a, b, _, shared in att_events if not shared]
+    solo_ms = statistics.fmean(a.elapsed_time(b) for a, b in solo) if solo else None
     flops_alone, att_ms_alone = attention_roofline(w, runner)
-    traffic = None
-    tp = ROOT / "profiles" / "fmha_traffic.json"
-    if tp.exists():
-        traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch")
+    traffic = attention_traffic()
+    kernels = kernel_table(ktimer, hbm, tflops_sustained, peak_kind)
     assert _lib.device_error() == 0, "device error word set during the benchmark"
+
+    # ---------------------------------------------------------------- C5 sharded batch (strong scaling)
+    c5 = None
+    if not args.no_c5:
+        del sol, runner
+        torch.cuda.empty_cache()
+        c5 = c5_bench(rank, ws, dev, dist, steps=args.c5_steps, warmup=1, model=model)
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -834,12 +901,15 @@ def main():
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "Solution.generate (pinned host voxels + fp16 DINO in, latents to host)"},
             "gpu_launches": int(launches),
-            "roofline": {"kernel": "fmha_fwd_kernel<128> (window self-attention, 4x4096 voxels, 12x128)",
+            "roofline": {"kernel": "attention_kernel<128> (window self-attention, 4x4096 voxels, 12x128)",
                          "bound": "tensor", "achieved": achieved, "peak": tflops_sustained, "unit": "TFLOP/s",
                          "frac": achieved / tflops_sustained,
                          "peak_kind": f"{peak_kind} sustained bf16 (kernel timed inside the timed steps)",
                          "flops_per_launch": flops, "ms_per_launch": live_ms, "launches": len(att_events),
                          "traffic": traffic,
+                         "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of "
+                                           "the same kernel source (profiles/attention_traffic.json)",
+                         "kernels": kernels,
                          "unshared": None if solo_ms is None else {
                              "ms_per_launch": solo_ms, "launches": len(solo),
                              "achieved": flops / (solo_ms / 1e3) / 1e12,
@@ -851,6 +921,7 @@ def main():
                                    "frac": flops_alone / (att_ms_alone / 1e3) / 1e12 / tflops_peak}},
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
+            "c5": c5,
         }), flush=True)
     if dist is not None:
         dist.barrier()

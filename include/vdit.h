@@ -141,6 +141,30 @@ int vdit_vec_ln_modulate(const float* v, int32_t d, const float* s1, const float
                          vdit_stream_t stream);
 int vdit_vec_gate_residual(float* c, const void* y, const float* g, int32_t d, vdit_stream_t stream);
 
+/* Batched matrix-vector products for the one-row linears: the context vector of the exact
+ * 1-token branch (the reference runs them as F.linear on a [1, D] row, lib/fast_flow.py:
+ * 1142-1156, 1702-1794, 2295-2309) and the time-embedding / gate MLP (lib/fast_flow.py:
+ * 455-654; BK/models/generators/lat_dit.py:631-635, 391-392, 409-410, 463-464, 817).
+ *   out[b][r] = act(sum_i W[b][r][i] * x'[b][i] + bias[b][r]),  r < n, i < k, b < batch
+ * x_mode selects the fused prologue that forms x' (fp32 accumulation throughout):
+ *   VDIT_GEMV_X_BF16    x bf16 [k]
+ *   VDIT_GEMV_X_F32     x fp32 [k]
+ *   VDIT_GEMV_X_LN_MOD  x fp32 [k]: x' = bf16(LN(x) * mod_scale + mod_shift), eps 1e-6
+ *   VDIT_GEMV_X_SWIGLU  x bf16 [2k] = [a | g]: x' = bf16(silu(g) * a)
+ * W is bf16 (w_f32 = 0) or fp32 [n, k] per batch entry, 16-byte aligned, k a multiple of 8
+ * (bf16) or 4 (fp32), k <= 8192; bias has W's type (or NULL).  out is bf16 or fp32 (out_f32)
+ * [n] per entry, silu applied when silu_out.  Strides between batch entries are in elements
+ * (x_bstride = 0 shares one input vector). */
+#define VDIT_GEMV_X_BF16 0
+#define VDIT_GEMV_X_F32 1
+#define VDIT_GEMV_X_LN_MOD 2
+#define VDIT_GEMV_X_SWIGLU 3
+int vdit_gemv(int32_t x_mode, const void* x, int64_t x_bstride, const float* mod_scale,
+              const float* mod_shift, int64_t mod_bstride, int32_t w_f32, const void* w,
+              int64_t w_bstride, const void* bias, int64_t bias_bstride, int32_t out_f32,
+              int32_t silu_out, void* out, int64_t out_bstride, int32_t n, int32_t k, int32_t batch,
+              vdit_stream_t stream);
+
 /* out[m,f] = silu(h[:, f:2f]) * h[:, :f] from packed h [m,2f] bf16.  Replaces
  * _fused_packed_swiglu_kernel (lib/fast_kernels.py:650-669, 942-974). */
 int vdit_swiglu_packed(const void* h, int64_t m, int32_t f, void* out, vdit_stream_t stream);
@@ -253,8 +277,8 @@ int vdit_dense_conv27(const void* f, int64_t n, int32_t cin, int32_t cout, const
  * nn.Linear of every block projection, BK/models/generators/lat_dit.py:306-345 (the
  * reference calls cuBLAS through F.linear with bf16 weights pre-cast,
  * lib/fast_flow.py:150-163).  a bf16 [m,lda], w bf16 [n,ldw], bias bf16 [n] or NULL,
- * out bf16 [m,ldo]; n a multiple of 128 or of 192, k % 64 == 0, leading dimensions
- * multiples of 8, pointers 16-byte aligned. */
+ * out bf16 [m,ldo]; n and k multiples of 8 (a partial last column tile or k-step reads
+ * zeros past n and k), leading dimensions multiples of 8, pointers 16-byte aligned. */
 int vdit_linear(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias, void* out,
                 int64_t ldo, int64_t m, int32_t n, int32_t k, vdit_stream_t stream);
 

@@ -20,3 +20,17 @@ Contents
 Parity of both modules is pinned against fixtures produced by running the
 reference itself on CPU (``tests/golden/make_golden.py``).
 """
+
+import os as _os
+from pathlib import Path as _Path
+
+
+def reference_root():
+    """The reference checkout named by the ``VDIT_REFERENCE_DIR`` environment variable, or
+    None (unset, or not a directory).  Fixture generators, the checker build and the tests
+    that read the reference's own files use it; there is no default location."""
+    v = _os.environ.get("VDIT_REFERENCE_DIR")
+    if not v:
+        return None
+    p = _Path(v)
+    return p if p.is_dir() else None

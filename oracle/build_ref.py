@@ -3,30 +3,35 @@
 Compiles ``oracle/ref_libsparse.cpp`` (our binding) with the reference's unmodified
 ``BK/ops/libsparse/conv.cu``, read where it lies in the reference checkout, for sm_100a
 into ``oracle/_ref/vdit_ref_libsparse.so`` (git-ignored; it is copied to GPU machines with
-the other built libraries).  Skipped when the checkout is absent.  The reference's own
+the other built libraries).  The checkout is an argument, else ``VDIT_REFERENCE_DIR``;
+without either the build is skipped.  The reference's own
 build system (its setup.py, which also pulls in its attention and mesh sources) is not
 used.
 
-    python oracle/build_ref.py
+    python oracle/build_ref.py <reference-root>
 """
 from __future__ import annotations
 
 import os
 import shutil
+import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF_CONV = Path("/root/reference/baseline_repo/3dgen-main/ops/libsparse/conv.cu")
+CONV_IN_CHECKOUT = Path("baseline_repo/3dgen-main/ops/libsparse/conv.cu")
 OUT_DIR = HERE / "_ref"
 OUT = OUT_DIR / "vdit_ref_libsparse.so"
 NAME = "vdit_ref_libsparse"
 
 
-def build(verbose: bool = False):
+def build(ref_root=None, verbose: bool = False):
     """Returns the built library's path, or None without the reference checkout."""
-    if not REF_CONV.exists():
+    if ref_root is None:
+        from oracle import reference_root
+        ref_root = reference_root()
+    if ref_root is None or not (Path(ref_root) / CONV_IN_CHECKOUT).exists():
         return None
-    sources = [HERE / "ref_libsparse.cpp", REF_CONV]
+    sources = [HERE / "ref_libsparse.cpp", Path(ref_root) / CONV_IN_CHECKOUT]
     if OUT.exists() and OUT.stat().st_mtime >= max(s.stat().st_mtime for s in sources):
         return OUT
     bdir = OUT_DIR / "build"
@@ -55,4 +60,5 @@ def load_built():
 
 
 if __name__ == "__main__":
-    print(build(verbose=True))
+    sys.path.insert(0, str(HERE.parent))
+    print(build(sys.argv[1] if len(sys.argv) > 1 else None, verbose=True))

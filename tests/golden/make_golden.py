@@ -2,7 +2,7 @@
 
 Usage (needs the reference checkout, read-only, and no GPU):
 
-    TORCHDYNAMO_DISABLE=1 python tests/golden/make_golden.py /root/reference
+    TORCHDYNAMO_DISABLE=1 python tests/golden/make_golden.py <reference-root>
 
 Writes ``tests/golden/golden.npz``.  Every array comes out of the reference's
 own code (its CPU fallbacks for the Triton/CUDA ops, installed by
@@ -234,4 +234,6 @@ def main(ref: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    if len(sys.argv) != 2:
+        raise SystemExit(__doc__)
+    main(Path(sys.argv[1]))

@@ -436,10 +436,13 @@ def test_dense_conv27_rejects_bad_shapes():
                                                  (4101, 1536, 4608, True, False), (16384, 1536, 1536, False, False),
                                                  (1000, 3840, 1536, True, True), (129, 128, 768, True, True),
                                                  (16384, 1536, 1536, True, True), (4101, 1536, 7680, True, False),
-                                                 (5000, 256, 576, True, False), (2000, 512, 640, False, True)])
+                                                 (5000, 256, 576, True, False), (2000, 512, 640, False, True),
+                                                 (300, 480, 960, True, False), (4101, 200, 320, True, True),
+                                                 (777, 72, 200, True, True), (1, 1536, 1536, True, False)])
 def test_linear_matches_fp32(m, k, n, bias, strided):
     """Pair tiles of 256, 192 or 128 columns, the widest that divides n (n = 576 takes
-    192-column tiles, n = 640 128-column tiles with the 8-stage ring)."""
+    192-column tiles, n = 640 128-column tiles with the 8-stage ring); a partial last
+    k-step (k = 480, 72, 200) and a partial last column tile (n = 320, 200) read zeros."""
     g = torch.Generator(device=DEV).manual_seed(m + k + n)
     a_full = torch.randn(m, k + (64 if strided else 0), device=DEV, generator=g).to(torch.bfloat16)
     a = a_full[:, 16:16 + k] if strided else a_full             # row stride k + 64, 32-byte offset
@@ -458,14 +461,79 @@ def test_linear_matches_fp32(m, k, n, bias, strided):
 
 def test_linear_rejects_bad_shapes():
     a = torch.zeros(10, 100, device=DEV, dtype=torch.bfloat16)
-    with pytest.raises(RuntimeError, match="unsupported"):
+    with pytest.raises(RuntimeError, match="unsupported"):            # k not a multiple of 8
         fk.linear(a, torch.zeros(256, 100, device=DEV, dtype=torch.bfloat16))
-    with pytest.raises(RuntimeError, match="unsupported"):
+    with pytest.raises(RuntimeError, match="unsupported"):            # n not a multiple of 8
         fk.linear(torch.zeros(10, 128, device=DEV, dtype=torch.bfloat16),
                   torch.zeros(100, 128, device=DEV, dtype=torch.bfloat16))
-    with pytest.raises(RuntimeError, match="unsupported"):          # 320: neither 128 nor 192 divides it
+    with pytest.raises(RuntimeError, match="unsupported"):
         fk.linear(torch.zeros(10, 128, device=DEV, dtype=torch.bfloat16),
-                  torch.zeros(320, 128, device=DEV, dtype=torch.bfloat16))
+                  torch.zeros(324, 128, device=DEV, dtype=torch.bfloat16))
+
+
+# ----------------------------------------------------------------------------- one-row linears (GEMV)
+
+def _ln_mod_ref(x, s1, sh):
+    mu = x.mean()
+    var = ((x - mu) ** 2).mean()
+    return ((x - mu) * torch.rsqrt(var + 1e-6) * s1 + sh).to(torch.bfloat16).float()
+
+
+@pytest.mark.parametrize("mode,wdt,n,k,batch,silu_out", [
+    (fk.GEMV_X_BF16, torch.bfloat16, 1536, 1536, 1, False),
+    (fk.GEMV_X_BF16, torch.bfloat16, 3072, 1536, 1, False),
+    (fk.GEMV_X_LN_MOD, torch.bfloat16, 3072, 1536, 1, False),
+    (fk.GEMV_X_LN_MOD, torch.bfloat16, 1536, 1536, 16, False),
+    (fk.GEMV_X_SWIGLU, torch.bfloat16, 1536, 3840, 1, False),
+    (fk.GEMV_X_F32, torch.float32, 6144, 256, 1, True),
+    (fk.GEMV_X_F32, torch.float32, 1536, 6144, 1, True),
+    (fk.GEMV_X_F32, torch.float32, 24 * 9 * 256, 256, 1, False),
+    (fk.GEMV_X_BF16, torch.bfloat16, 40, 104, 3, False),
+    (fk.GEMV_X_F32, torch.float32, 7, 12, 1, False),
+])
+def test_gemv_matches_fp32(mode, wdt, n, k, batch, silu_out):
+    """Every prologue (plain bf16 / fp32 vector, LayerNorm-modulated fp32 vector with
+    per-entry scale and shift, SwiGLU of a packed bf16 vector), bf16 and fp32 weights,
+    batches, short rows (k = 12, 104: fewer chunks than lanes)."""
+    g = torch.Generator(device=DEV).manual_seed(n + k + batch)
+    w = (0.03 * torch.randn(batch, n, k, device=DEV, generator=g)).to(wdt)
+    b = (0.1 * torch.randn(batch, n, device=DEV, generator=g)).to(wdt)
+    s1 = 1 + 0.2 * torch.randn(batch, 2, k, device=DEV, generator=g)
+    if mode == fk.GEMV_X_SWIGLU:
+        x = torch.randn(2 * k, device=DEV, generator=g).to(torch.bfloat16)
+        xr = (torch.nn.functional.silu(x[k:].float()) * x[:k].float()).to(torch.bfloat16).float()
+    elif mode == fk.GEMV_X_BF16:
+        x = torch.randn(k, device=DEV, generator=g).to(torch.bfloat16)
+        xr = x.float()
+    else:
+        x = 3 + torch.randn(k, device=DEV, generator=g)
+        xr = x
+    xs = [xr] * batch
+    if mode == fk.GEMV_X_LN_MOD:
+        xs = [_ln_mod_ref(x, s1[i, 0], s1[i, 1]) for i in range(batch)]
+    ww = w if batch > 1 else w[0]
+    bb = b if batch > 1 else b[0]
+    kw = dict(x_mode=mode, out_dtype=torch.float32 if wdt == torch.float32 else torch.bfloat16, silu_out=silu_out)
+    if mode == fk.GEMV_X_LN_MOD:
+        kw.update(mod_scale=s1[:, 0] if batch > 1 else s1[0, 0], mod_shift=s1[:, 1] if batch > 1 else s1[0, 1])
+    out = fk.gemv(x, ww, bb, **kw)
+    ref = torch.stack([w[i].float() @ xs[i] + b[i].float() for i in range(batch)])
+    if silu_out:
+        ref = torch.nn.functional.silu(ref)
+    out = out.reshape(batch, n)
+    tol = 1e-5 if wdt == torch.float32 else 5e-3                  # fp32 / bf16 output rounding
+    assert rel(out, ref) < tol
+
+
+def test_gemv_rejects_bad_arguments():
+    w = torch.zeros(64, 1536, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        fk.gemv(torch.zeros(1500, device=DEV, dtype=torch.bfloat16), w)
+    with pytest.raises(ValueError):
+        fk.gemv(torch.zeros(1536, device=DEV), w, x_mode=fk.GEMV_X_LN_MOD)
+    with pytest.raises(RuntimeError, match="unsupported"):
+        fk.gemv(torch.zeros(9000, device=DEV, dtype=torch.bfloat16),
+                torch.zeros(8, 9000, device=DEV, dtype=torch.bfloat16))
 
 
 @pytest.mark.parametrize("n,heads,hd,res", [(3000, 12, 128, 128), (16384, 12, 128, 64), (300, 2, 128, 64),

@@ -9,7 +9,10 @@ import torch
 
 from vdit import ingest
 
-REF_SAMPLES = Path("/root/reference/fetched_info/sample_test_data/public_test")
+from oracle import reference_root
+
+_REF = reference_root()
+REF_SAMPLES = _REF / "fetched_info" / "sample_test_data" / "public_test" if _REF else Path("/nonexistent")
 
 
 def _write_sample(root: Path, sid: str, n: int, view: str = "4view_000", key: str = "vox_idxi", cache=True):
@@ -56,7 +59,7 @@ def test_lookup_order_and_fallbacks(tmp_path):
         ingest.load_vox_idxi(e / "bad.npz")
 
 
-@pytest.mark.skipif(not REF_SAMPLES.is_dir(), reason="the reference checkout is not present")
+@pytest.mark.skipif(not REF_SAMPLES.is_dir(), reason="VDIT_REFERENCE_DIR does not name a reference checkout")
 def test_reference_public_samples_in_place():
     ids = ingest.list_samples(REF_SAMPLES)
     assert ids, "no public-test sample with 4view_000 features"

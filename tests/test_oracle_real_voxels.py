@@ -17,10 +17,12 @@ import torch
 
 from oracle import geometry as geo
 
-REF = Path(os.environ.get("VDIT_REFERENCE_DIR", "/root/reference"))
-SAMPLES = sorted((REF / "fetched_info" / "sample_test_data" / "public_test").glob("*/cache/vox_idxi.npz"))
+from oracle import reference_root
 
-pytestmark = pytest.mark.skipif(not SAMPLES, reason="reference checkout with the public-test samples not present")
+REF = reference_root()
+SAMPLES = sorted((REF / "fetched_info" / "sample_test_data" / "public_test").glob("*/cache/vox_idxi.npz")) if REF else []
+
+pytestmark = pytest.mark.skipif(not SAMPLES, reason="VDIT_REFERENCE_DIR does not name a reference checkout")
 
 
 @pytest.fixture(scope="module")
