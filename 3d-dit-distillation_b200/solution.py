@@ -2,9 +2,9 @@
 
 Same contract as the reference's ``solution.py:135-246``:
 ``from_pretrained(path, device=None, torch_dtype=None, **kw)`` discovers the
-weights (``path``, ``path/lat_dit``, ``$LAT_DIT_DIR``, ``$LAT_DIT_WEIGHTS_DIR``,
-``$KANDI3D_WEIGHTS_DIR``, ``--lat-dit-dir`` on argv, ``solution.py:48-102``),
-loads config + solver config, builds the runner and warms it up;
+weights in the reference's order (``solution.py:48-102``), loads config + solver
+config, folds a distilled adapter found beside the weights into them
+(``solution.py:105-132``, called at ``:205``), builds the runner and warms it up;
 ``generate_impl`` returns one [N_i, 16] fp32 latent tensor per sample, in the
 caller's voxel order.  ``generate()`` is inherited and never overridden.
 Batches run sample by sample (each sample owns its geometry).
@@ -15,7 +15,7 @@ import json
 import os
 import sys
 from pathlib import Path
-from typing import Any, Optional, Union
+from typing import Any, Dict, Optional, Sequence, Union
 
 import torch
 
@@ -24,26 +24,91 @@ from .fast_sampler import SolverConfig
 from .model import LatDitModel
 from .runtime import FlowMatchSamplingParams, LatDitConditioning, LatDitGenerator, resolve
 
+# Organiser locations the reference tries last, relative to the working directory
+# unless absolute (``solution.py:91-100``).
+DEFAULT_WEIGHT_LOCATIONS = ("weights/lat_dit", "kandi3d_weights_aijc_kit/lat_dit", "../weights/lat_dit",
+                            "/weights/lat_dit", "/workspace/weights/lat_dit")
+
 
 def _has_weights(d: Path) -> bool:
     return (d / "diffusion_pytorch_model.safetensors").is_file() or (d / "diffusion_pytorch_model.bin").is_file()
 
 
-def _discover_weights_dir(primary: Path) -> Path:
-    cands = [primary, primary / "lat_dit"]
-    argv = sys.argv
-    if "--lat-dit-dir" in argv:
-        i = argv.index("--lat-dit-dir")
-        if i + 1 < len(argv):
-            cands.append(Path(argv[i + 1]))
+def _dir_or_lat_dit(c: Path) -> Optional[Path]:
+    if _has_weights(c):
+        return c
+    if _has_weights(c / "lat_dit"):
+        return c / "lat_dit"
+    return None
+
+
+def _discover_weights_dir(primary: Path, argv: Optional[Sequence[str]] = None,
+                          environ: Optional[Dict[str, str]] = None) -> Path:
+    """The directory holding ``diffusion_pytorch_model.safetensors`` (or ``.bin``), searched
+    in the reference's order (``solution.py:48-102``): ``primary`` and ``primary/lat_dit``;
+    then, scanning the command line, ``--lat-dit-dir X`` / ``--lat-dit-dir=X`` (X or
+    X/lat_dit) and ``--lat-vae-dir X`` / ``--lat-vae-dir=X`` (the ``lat_dit`` directory beside
+    X); then ``$LAT_DIT_DIR``, ``$LAT_DIT_WEIGHTS_DIR``, ``$KANDI3D_WEIGHTS_DIR`` (each as is
+    or its ``lat_dit``); then the organiser locations.  Falls back to ``primary``."""
+    argv = sys.argv if argv is None else argv
+    environ = os.environ if environ is None else environ
+    hit = _dir_or_lat_dit(primary)
+    if hit is not None:
+        return hit
+    for i, arg in enumerate(argv):
+        if arg == "--lat-dit-dir" and i + 1 < len(argv):
+            hit = _dir_or_lat_dit(Path(argv[i + 1]).expanduser().resolve())
+        elif arg.startswith("--lat-dit-dir="):
+            hit = _dir_or_lat_dit(Path(arg.split("=", 1)[1]).expanduser().resolve())
+        elif arg == "--lat-vae-dir" and i + 1 < len(argv):
+            c = Path(argv[i + 1]).expanduser().resolve().parent / "lat_dit"
+            hit = c if _has_weights(c) else None
+        elif arg.startswith("--lat-vae-dir="):
+            c = Path(arg.split("=", 1)[1]).expanduser().resolve().parent / "lat_dit"
+            hit = c if _has_weights(c) else None
+        if hit is not None:
+            return hit
     for env in ("LAT_DIT_DIR", "LAT_DIT_WEIGHTS_DIR", "KANDI3D_WEIGHTS_DIR"):
-        if os.environ.get(env):
-            p = Path(os.environ[env])
-            cands += [p, p / "lat_dit"]
-    for c in cands:
-        if _has_weights(c):
-            return c
+        v = environ.get(env)
+        if v:
+            hit = _dir_or_lat_dit(Path(v).expanduser().resolve())
+            if hit is not None:
+                return hit
+    for rel in DEFAULT_WEIGHT_LOCATIONS:
+        if _has_weights(Path(rel)):
+            return Path(rel).resolve()
     return primary
+
+
+def merge_distilled_adapters(state: Dict[str, torch.Tensor], custom_dir: Path) -> int:
+    """Fold a distilled adapter (``custom_dir/student_adapter.pt``) into the checkpoint
+    tensors, as the reference does at load (``solution.py:105-132``): for every LoRA pair
+    ``W += (B @ A) * lora_scale`` (``lora_scale`` default 1), then ``W += delta`` for every
+    entry of ``weight_deltas``; keys absent from the checkpoint are skipped, an unreadable
+    file is ignored.  The sums are taken in fp32 and the folded tensors stay fp32 (the
+    reference's parameters are fp32).  Returns the number of tensors changed."""
+    adapter = Path(custom_dir) / "student_adapter.pt"
+    if not adapter.is_file():
+        return 0
+    try:
+        payload = torch.load(adapter, map_location="cpu", weights_only=True)
+    except Exception:          # the reference ignores an adapter it cannot read
+        return 0
+    changed = 0
+    scale = float(payload.get("lora_scale", 1.0))
+    lora_b = payload.get("lora_B", {})
+    for key, a in payload.get("lora_A", {}).items():
+        b = lora_b.get(key)
+        if b is not None and key in state:
+            w = state[key]
+            state[key] = w.float() + ((b.float() @ a.float()) * scale).to(w.device)
+            changed += 1
+    for key, delta in payload.get("weight_deltas", {}).items():
+        if key in state:
+            w = state[key]
+            state[key] = w.float() + delta.float().to(w.device)
+            changed += 1
+    return changed
 
 
 class Solution(LatDitGenerator):
@@ -74,6 +139,7 @@ class Solution(LatDitGenerator):
         model = LatDitModel.from_pretrained(wdir) if _has_weights(wdir) else None
         if model is None:
             raise FileNotFoundError(f"no diffusion_pytorch_model.safetensors or .bin found for {primary}")
+        merge_distilled_adapters(model.state, primary)
         solver = SolverConfig.from_dir(primary, fallback_model_cfg=mc)
         if device is not None:
             device = torch.device(f"cuda:{device}" if isinstance(device, int) else device)
@@ -112,4 +178,4 @@ class Solution(LatDitGenerator):
         return outs
 
 
-__all__ = ["Solution"]
+__all__ = ["Solution", "merge_distilled_adapters"]
