@@ -3,6 +3,7 @@
 // K and V (2 * n * heads * head_dim bf16), so it is HBM-bound: split-K over
 // many blocks, 16-byte loads, online softmax in fp32, partial states
 // (max, sum, o[head_dim]) in the caller's workspace, then a combine kernel.
+#include <cuda.h>
 #include <math.h>
 
 #include <mutex>
@@ -162,10 +163,33 @@ __device__ __align__(256) float g_attn1q_scratch[kNoAllocScratchFloats];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
-float* g_scratch_addr[kMaxDevices] = {};
+struct ScratchEntry {
+    CUcontext ctx;        // the context the address was looked up in
+    float* addr;
+};
+ScratchEntry g_scratch[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device, looked up once per
-// device (the host-side symbol is not a device address and must not reach a kernel).
+// The current driver context (null when the driver entry point is unavailable): a
+// device reset or a context destroyed and re-created reloads the module, which moves
+// the array, so a cached address is only valid in the context it was looked up in.
+CUcontext current_context() {
+    using Fn = CUresult (*)(CUcontext*);
+    static Fn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<Fn>(p);
+    });
+    CUcontext c = nullptr;
+    if (fn && fn(&c) != CUDA_SUCCESS) c = nullptr;
+    return c;
+}
+
+// Device address of the scratch array on the current device, looked up once per device
+// and context (the host-side symbol is not a device address and must not reach a kernel).
 int scratch_address(float** addr) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
@@ -174,17 +198,20 @@ int scratch_address(float** addr) {
         return VDIT_ERR_LAUNCH;
     }
     if (dev < 0 || dev >= kMaxDevices) return VDIT_ERR_UNSUPPORTED;
+    const CUcontext ctx = current_context();
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (g_scratch_addr[dev] == nullptr) {
+    ScratchEntry& ent = g_scratch[dev];
+    if (ent.addr == nullptr || ctx == nullptr || ent.ctx != ctx) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_attn1q_scratch);
         if (e != cudaSuccess) {
             record_cuda_error(e);
             return VDIT_ERR_LAUNCH;
         }
-        g_scratch_addr[dev] = static_cast<float*>(p);
+        ent.addr = static_cast<float*>(p);
+        ent.ctx = ctx;
     }
-    *addr = g_scratch_addr[dev];
+    *addr = ent.addr;
     return VDIT_OK;
 }
 

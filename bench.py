@@ -190,6 +190,51 @@ def attention_roofline(w, runner, reps: int = 20):
     return flops, ms
 
 
+def vendor_attention_bars(w, reps: int = 20) -> dict:
+    """Library attention on the same window self-attention shapes (four 4096-voxel windows,
+    12 x 128 heads, bf16), reported beside the kernel only: torch SDPA with the cuDNN and
+    the flash backends, and the flash_attn package's varlen packed-QKV entry point (the
+    reference's attention backend, ``lib/fast_kernels.py:1538-1587``).  CUDA events; a
+    backend that does not run on this GPU is reported with its error."""
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    D, H, HD = w.arch.dim, w.arch.heads, w.arch.head_dim
+    nwin = w.n // 4096
+    g = torch.Generator(device="cuda").manual_seed(1)
+    q, k, v = (torch.randn(nwin, H, 4096, HD, device="cuda", generator=g).to(torch.bfloat16) for _ in range(3))
+    flops = 4.0 * nwin * 4096 * 4096 * D
+    s = torch.cuda.current_stream()
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(reps):
+            fn()
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        return {"ms_per_launch": ms, "tflops": flops / ms / 1e9}
+
+    out = {}
+    for name, backend in (("sdpa_cudnn", SDPBackend.CUDNN_ATTENTION), ("sdpa_flash", SDPBackend.FLASH_ATTENTION)):
+        try:
+            with sdpa_kernel([backend]):
+                out[name] = timed(lambda: F.scaled_dot_product_attention(q, k, v))
+        except Exception as exc:  # a backend without sm_100 support
+            out[name] = {"error": f"{type(exc).__name__}: {str(exc)[:160]}"}
+    try:
+        from flash_attn import flash_attn_varlen_qkvpacked_func
+        qkv = torch.stack([q, k, v], 2).permute(0, 3, 2, 1, 4).reshape(nwin * 4096, 3, H, HD).contiguous()
+        cu = torch.arange(0, nwin + 1, device="cuda", dtype=torch.int32) * 4096
+        out["flash_attn_varlen_qkvpacked"] = timed(lambda: flash_attn_varlen_qkvpacked_func(qkv, cu, 4096))
+    except Exception as exc:
+        out["flash_attn_varlen_qkvpacked"] = {"error": f"{type(exc).__name__}: {str(exc)[:160]}"}
+    return out
+
+
 def dwconv_roofline(w, reps: int = 20):
     """Average duration of the depthwise conv + SwiGLU kernel on the workload's shapes
     (N=16384 shell voxels, 7680 -> 3840 channels), CUDA events on its stream.
@@ -722,7 +767,8 @@ def main():
         return
     if args.only == "attention":
         flops, ms = attention_roofline(w, None)
-        print(json.dumps({"kernel": "attention_kernel<128>", "ms_per_launch": ms, "tflops": flops / ms / 1e9}))
+        print(json.dumps({"kernel": "attention_kernel<128>", "ms_per_launch": ms, "tflops": flops / ms / 1e9,
+                          "library": vendor_attention_bars(w)}))
         return
     if args.only == "qknorm":
         print(json.dumps(qknorm_bench(w)))

@@ -239,8 +239,9 @@ int vdit_attention_1q(const void* q, const void* k, const void* v, int64_t kv_st
  * partials live in a fixed 1 MiB device array inside the library (one per GPU
  * that loads it, kept until process exit); heads * splits * (head_dim + 2) fp32
  * values must fit, else VDIT_ERR_TOO_LARGE (12 heads x 128 fits any n_keys).
- * The first call on a device looks up the array's device address (make that
- * call before any stream capture).  Calls share the array: calls that overlap
+ * The first call on a device, and the first call after that device's context was
+ * re-created (a device reset), looks up the array's device address (make that call
+ * before any stream capture).  Calls share the array: calls that overlap
  * on the GPU (different streams, or different threads on one device) race.
  * Allocates nothing; q, k, v, out as for vdit_attention_1q. */
 int vdit_attention_1q_noalloc(const void* q, const void* k, const void* v, int64_t kv_stride,

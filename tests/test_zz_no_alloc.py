@@ -53,6 +53,41 @@ def test_noalloc_matches_workspace_entry_point(n, heads, hd):
     assert _lib.device_error() == 0
 
 
+def test_noalloc_padded_kv_rows():
+    """K/V rows with a stride beyond 2 * heads * head_dim (padded rows)."""
+    heads, hd, n = 12, 128, 3000
+    d = heads * hd
+    g = torch.Generator(device=DEV).manual_seed(7)
+    q = torch.randn(d, device=DEV, generator=g)
+    kv = torch.randn(n, 2 * d + 64, device=DEV, generator=g).to(torch.bfloat16)[:, :2 * d]
+    assert kv.stride(0) == 2 * d + 64
+    ref = fk.attention_1q(q, kv, heads, hd)
+    for _ in range(2):
+        rc, out = noalloc_1q(q, kv, heads, hd)
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert rel(out, ref) < 1e-2
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_noalloc_on_a_second_device():
+    """Each GPU holds its own array and the library looks up its address per device: a
+    call on cuda:1 after calls on cuda:0 matches the workspace entry point there."""
+    heads, hd, n = 12, 128, 5000
+    d = heads * hd
+    for dev in ("cuda:0", "cuda:1", "cuda:0"):
+        with torch.cuda.device(dev):
+            g = torch.Generator(device=dev).manual_seed(11)
+            q = torch.randn(d, device=dev, generator=g)
+            kv = torch.randn(n, 2 * d, device=dev, generator=g).to(torch.bfloat16)
+            ref = fk.attention_1q(q, kv, heads, hd)
+            rc, out = noalloc_1q(q, kv, heads, hd)
+            assert rc == 0
+            torch.cuda.synchronize()
+            assert rel(out, ref) < 1e-2
+            assert _lib.device_error() == 0
+
+
 def test_noalloc_refuses_sizes_beyond_its_scratch():
     heads, hd = 2048, 128                    # heads * splits * (hd + 2) floats > 1 MiB
     kv = torch.zeros(1, 2 * heads * hd, device=DEV, dtype=torch.bfloat16)
