@@ -62,6 +62,10 @@ SIGNATURES = {
     "vdit_linear_qkv_rope3d": (ctypes.c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _vp, _vp, _vp, _vp, _c_i32, _vp, _vp,
                                               _vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _vp]),
     "vdit_gather_rows_f32": (ctypes.c_int, [_vp, _vp, _c_i64, _c_i32, _vp, _vp]),
+    "vdit_cfg_reuse_workspace_bytes": (_c_sz, []),
+    "vdit_cfg_reuse_euler": (ctypes.c_int, [_vp, _vp, _vp, _vp, _c_i64, _c_f32, _c_f32, _c_f32, _c_f32, _c_f32, _c_i32,
+                                            _vp, _c_sz, _vp]),
+    "vdit_neg_endpoint": (ctypes.c_int, [_vp, _vp, _c_i64, _c_f32, _vp, _vp]),
     "vdit_cfg_euler": (ctypes.c_int, [_vp, _vp, _vp, _c_i64, _c_f32, _c_f32, _vp]),
     "vdit_unpermute_denorm": (ctypes.c_int, [_vp, _vp, _c_i64, _vp, _vp, _vp, _vp]),
 }

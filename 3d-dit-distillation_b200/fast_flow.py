@@ -28,7 +28,7 @@ from typing import Any, Dict, List, Optional
 import torch
 
 from . import fast_kernels as fk
-from .fast_sampler import SolverConfig, build_schedule
+from .fast_sampler import SolverConfig, build_schedule, should_eval_uncond
 from .model import LatDitArch, LatDitModel
 from .runtime import FlowMatchSamplingParams, LatDitConditioning
 
@@ -114,6 +114,9 @@ class OptimizedLatDitRunner:
         # in its epilogue (tcgen05 GEMM) where the head layout allows (head_dim 96 or 128,
         # an even number of heads: a pair tile holds two whole heads of one section)
         self.fused_qkv = self.head_dim in (96, 128) and self.num_heads % 2 == 0
+        # the 1-token branch's single query over the voxel rows without forming K/V takes up to
+        # 16 heads and a width that is a multiple of 128 (at most 2048); other widths form K/V
+        self._wide_1q = self.num_heads <= 16 and self.dim % 128 == 0 and self.dim <= 2048 and self.head_dim <= 256
         # CUDA-graph replay of the sampler (per voxel count, context length and schedule)
         self.cuda_graph = bool(cuda_graph)
         self._graphs: "OrderedDict[tuple, _SampleGraph]" = OrderedDict()
@@ -530,8 +533,13 @@ class OptimizedLatDitRunner:
                     if two:
                         side.wait_event(kv_ready)
                         h_kv.record_stream(side)
-                    o1 = self._run("single_query_context_to_voxel", h_kv.numel() * 2.0 + w["kvx_w"].numel() * 2.0,
-                                   fk.attention_1q_wide, q_cc, h_kv, w["kvx_w"], w["kvx_b"], H, HD)   # bf16 [D]
+                    if self._wide_1q:
+                        o1 = self._run("single_query_context_to_voxel", h_kv.numel() * 2.0 + w["kvx_w"].numel() * 2.0,
+                                       fk.attention_1q_wide, q_cc, h_kv, w["kvx_w"], w["kvx_b"], H, HD)   # bf16 [D]
+                    else:
+                        # widths the fused single query does not take: form K/V, then one query per head
+                        kv = self._lin(h_kv, w["kvx_w"], w["kvx_b"])
+                        o1 = fk.attention_1q(q_cc, kv, H, HD)
                     fk.vec_gate_residual_(c, fk.gemv(o1, w["cond_to_out_cross"], w["cond_to_out_cross_b"]), CG[5])
                     a_g = mod_lin(CG[6], CG[7], "cond_ffn0", "cond_ffn0_b", w)    # bf16 [2F]
                     # cond_ffn1(silu(g) * a): the SwiGLU of the packed vector runs in the GEMV prologue
@@ -594,7 +602,9 @@ class OptimizedLatDitRunner:
         use_graph = self.cuda_graph if cuda_graph is None else bool(cuda_graph)
         if not use_graph:
             return self._sample_steps(geom, context, noise, tl, guided, g_scale)
-        key = (N, int(context.shape[-2]), tuple(tl), tuple(guided), g_scale)
+        sc = self.solver_config
+        key = (N, int(context.shape[-2]), tuple(tl), tuple(guided), g_scale, sc.approximate_cfg_cache,
+               tuple(sc.eval_uncond_steps), sc.cfg_stride)
         entry = self._graphs.get(key)
         if entry is None:
             entry = self._capture_sample(key, geom, context, noise, tl, guided, g_scale)
@@ -632,6 +642,8 @@ class OptimizedLatDitRunner:
         Both ranks return the same latents ([N, 16] fp32, input voxel order)."""
         import torch.distributed as dist
         from . import distributed as vd
+        if self.solver_config.approximate_cfg_cache:
+            raise NotImplementedError("the two-GPU branch split runs the exact solver only (cfg_cache_mode 'exact')")
         geom = self._prepare_sample_geometry([vox], context)
         N = geom["N"]
         rank = dist.get_rank(group)
@@ -653,25 +665,48 @@ class OptimizedLatDitRunner:
 
     def _sample_steps(self, geom: Dict[str, Any], context: torch.Tensor, noise: torch.Tensor, tl: List[float],
                       guided: List[bool], g_scale: float) -> torch.Tensor:
-        """GPU part of the sampler: Euler + CFG over the schedule, latents in input order."""
+        """GPU part of the sampler: Euler + CFG over the schedule, latents in input order.
+        With the approximate CFG cache on (``SolverConfig.cfg_cache_mode == "neg_reuse"``), a
+        guided step that ``should_eval_uncond`` skips reuses the last unconditional velocity
+        (``lib/fast_flow.py:2791-2887``, non-QAOA branch); otherwise every guided step runs both
+        NFEs (the exact solver)."""
         xt = fk.gather_rows_f32(noise, geom["perm"])
         main = torch.cuda.current_stream(self.device)
+        sc = self.solver_config
+        approx = sc.approximate_cfg_cache
+        n_guided = sum(1 for g in guided if g)
+        last_neg = last_neg_x0 = None
         for i in range(len(guided)):
             both = guided[i] and g_scale > 0
-            neg = self._negative_stream() if (both and self.overlap_branches) else main
+            eval_neg = both and (not approx or last_neg is None or
+                                 should_eval_uncond(i, n_guided, sc.cfg_stride, sc.cfg_cache_mode,
+                                                    sc.eval_uncond_steps))
+            neg = self._negative_stream() if (eval_neg and self.overlap_branches) else main
             if neg is not main:
                 neg.wait_stream(main)                     # x_t of this step
                 xt.record_stream(neg)
             self._nfe_shared = neg is not main
             v = self.forward_flow_fast(xt, tl[i], context, None, geom)
             vn = None
-            if both:
+            if eval_neg:
                 with torch.cuda.stream(neg):
                     vn = self.forward_flow_fast(xt, tl[i], context, None, geom, uncond=True)
                 if neg is not main:
                     main.wait_stream(neg)
                     vn.record_stream(main)
-            fk.cfg_euler_(xt, v, vn, g_scale, tl[i] - tl[i + 1])
+            t_eval, dt = tl[i], tl[i] - tl[i + 1]
+            if both and not eval_neg:
+                blend = sc.autotarget_clean_endpoint_blend
+                x0 = last_neg_x0 if (blend > 0.0 and t_eval > 0.25) else None
+                hf = (sc.fastercache_hf_boost * max(0.0, 1.0 - t_eval)
+                      if (sc.fastercache_freq_decoupled_cfg and xt.shape[0] > 1) else 0.0)
+                fk.cfg_reuse_euler_(xt, v, last_neg, x0, g_scale, dt, t_eval, blend, hf, sc.cfg_zero_star_projection)
+            else:
+                if approx and eval_neg:
+                    last_neg = vn
+                    if sc.autotarget_clean_endpoint_blend > 0.0:
+                        last_neg_x0 = fk.neg_endpoint(xt, vn, t_eval)
+                fk.cfg_euler_(xt, v, vn, g_scale, dt)
         self._nfe_shared = False
         self._b0_share = None
         return fk.unpermute_denorm(xt, geom["up_widx"], self._denorm_scale, self._denorm_shift)

@@ -542,6 +542,30 @@ def cfg_euler_(xt: torch.Tensor, v_pos: torch.Tensor, v_neg: Optional[torch.Tens
     return xt
 
 
+def cfg_reuse_euler_(xt: torch.Tensor, v_pos: torch.Tensor, last_neg: torch.Tensor,
+                     last_neg_x0: Optional[torch.Tensor], guidance: float, dt: float, t_eval: float,
+                     endpoint_blend: float, hf_gain: float, zero_star: bool) -> torch.Tensor:
+    """Euler step of a guided step that reuses the last unconditional velocity (the
+    reference's approximate ``neg_reuse`` CFG cache, ``lib/fast_flow.py:2844-2887``): CFG-Zero*
+    projection, clean-endpoint blend (``last_neg_x0``, None to skip it) and high-frequency
+    boost; xt [N, 16] fp32 updated in place."""
+    for t, name in ((xt, "xt"), (v_pos, "v_pos"), (last_neg, "last_neg"), (last_neg_x0, "last_neg_x0")):
+        if t is not None and (t.dtype != torch.float32 or t.shape != xt.shape or not t.is_contiguous()):
+            raise ValueError(f"cfg_reuse_euler_: {name} must be contiguous fp32 {tuple(xt.shape)}")
+    ws = torch.empty(int(lib().vdit_cfg_reuse_workspace_bytes()), dtype=torch.uint8, device=xt.device)
+    check(lib().vdit_cfg_reuse_euler(ptr(xt), ptr(v_pos), ptr(last_neg), ptr(last_neg_x0), xt.shape[0],
+                                     float(guidance), float(dt), float(t_eval), float(endpoint_blend), float(hf_gain),
+                                     int(bool(zero_star)), ptr(ws), ws.numel(), _s(xt)), "cfg_reuse_euler")
+    return xt
+
+
+def neg_endpoint(xt: torch.Tensor, v_neg: torch.Tensor, t_eval: float) -> torch.Tensor:
+    """x0 = xt - t_eval * v_neg ([N, 16] fp32): the clean endpoint the CFG cache blends toward."""
+    out = torch.empty_like(xt)
+    check(lib().vdit_neg_endpoint(ptr(xt), ptr(v_neg), xt.shape[0], float(t_eval), ptr(out), _s(xt)), "neg_endpoint")
+    return out
+
+
 def unpermute_denorm(xt: torch.Tensor, up_widx: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor) -> torch.Tensor:
     out = torch.empty_like(xt)
     check(lib().vdit_unpermute_denorm(ptr(xt), ptr(up_widx), xt.shape[0], ptr(scale), ptr(shift), ptr(out), _s(xt)),

@@ -40,15 +40,38 @@ class SolverConfig:
     warmup_on_load: bool = True
     eval_cond_steps: List[int] = field(default_factory=list)
     eval_uncond_steps: List[int] = field(default_factory=list)
+    # the approximate CFG cache ("neg_reuse"), opt-in; the reference's defaults
+    # (lib/fast_sampler.py:25-79) apply once cfg_cache_mode is "neg_reuse"
+    cfg_zero_star_projection: bool = True
+    autotarget_clean_endpoint_blend: float = 0.08
+    fastercache_freq_decoupled_cfg: bool = True
+    fastercache_hf_boost: float = 0.035
     approximate_fields_ignored: List[str] = field(default_factory=list)
 
     _APPROX_FLAGS = ("qaoa_enabled", "mid_block_cache_enabled")
 
+    @property
+    def approximate_cfg_cache(self) -> bool:
+        """True when guided steps may reuse the last unconditional velocity."""
+        return self.cfg_cache_mode == "neg_reuse"
+
+    def enable_approximate_cfg_cache(self, eval_uncond_steps: Optional[List[int]] = None,
+                                     cfg_stride: int = 2) -> "SolverConfig":
+        """Switch on the reference's default approximate CFG cache (``cfg_cache_mode
+        "neg_reuse"``, unconditional NFE only at ``eval_uncond_steps``, default [0, 2])."""
+        self.cfg_cache_mode = "neg_reuse"
+        self.cfg_stride = int(cfg_stride)
+        self.eval_uncond_steps = list(eval_uncond_steps) if eval_uncond_steps is not None else [0, 2]
+        return self
+
     @classmethod
     def from_dir(cls, weights_dir: Optional[Path] = None,
-                 fallback_model_cfg: Optional[Dict[str, Any]] = None) -> "SolverConfig":
+                 fallback_model_cfg: Optional[Dict[str, Any]] = None,
+                 allow_approximate_cfg_cache: bool = False) -> "SolverConfig":
         """Defaults <- model config (cfg, cfg_range, rescale_t) <- weights_dir/solver_config.json
-        <- env LAT_DIT_STEPS / LAT_DIT_SOLVER (``lib/fast_sampler.py:163-203``)."""
+        <- env LAT_DIT_STEPS / LAT_DIT_SOLVER (``lib/fast_sampler.py:163-203``).  A config that
+        asks for the approximate CFG cache ("neg_reuse", cfg_stride, eval_uncond_steps) keeps it
+        only with ``allow_approximate_cfg_cache``; otherwise it is listed as ignored."""
         cfg = cls()
         if fallback_model_cfg:
             if "cfg" in fallback_model_cfg:
@@ -72,11 +95,15 @@ class SolverConfig:
                     if k == "solver_type" and v not in ("euler", "piecewise_euler"):
                         cfg.approximate_fields_ignored.append(f"solver_type={v}")
                         continue
-                    if k == "cfg_cache_mode" and v != "exact":
+                    approx_ok = allow_approximate_cfg_cache and data.get("cfg_cache_mode") == "neg_reuse"
+                    if k == "cfg_cache_mode" and v != "exact" and not (approx_ok and v == "neg_reuse"):
                         cfg.approximate_fields_ignored.append(f"cfg_cache_mode={v}")
                         continue
-                    if k == "cfg_stride" and int(v) != 1:
+                    if k == "cfg_stride" and int(v) != 1 and not approx_ok:
                         cfg.approximate_fields_ignored.append(f"cfg_stride={v}")
+                        continue
+                    if k == "eval_uncond_steps" and v and not approx_ok:
+                        cfg.approximate_fields_ignored.append(f"eval_uncond_steps={v}")
                         continue
                     setattr(cfg, k, (float(v[0]), float(v[1])) if k == "cfg_range" else v)
         if "LAT_DIT_STEPS" in os.environ:

@@ -682,6 +682,48 @@ def c5_bench(rank: int, ws: int, dev, dist, samples: int = 0, steps: int = 1, wa
         "gpu_launches": int(launches), "clocks": clk.summary()}
 
 
+def cfg_cache_bench(w, reps: int = 5) -> dict:
+    """Quality and speed of the approximate CFG cache on the C4 workload (the reference's
+    "neg_reuse" defaults: unconditional NFE at guided steps 0 and 2 only, 6 NFE per sample
+    instead of 7) against the exact solver: ms per sample (CUDA events, L2 flushed before each
+    sample) and the relative L2 distance of the final latents from the exact ones."""
+    from vdit.fast_flow import OptimizedLatDitRunner
+    from vdit.fast_sampler import SolverConfig
+    from vdit.model import LatDitModel
+    dev = torch.device("cuda", torch.cuda.current_device())
+    model = LatDitModel.random(w.arch, seed=0, device=dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    s = torch.cuda.current_stream()
+    out = {"workload": "C4 (24 blocks, N=16384, 4101 context tokens, CFG 3.0)"}
+    lats = {}
+    for mode in ("exact", "neg_reuse"):
+        solver = SolverConfig(num_inference_steps=4, n_guided_steps=3, n_unguided_steps=1, guidance_scale=w.guidance)
+        if mode == "neg_reuse":
+            solver.enable_approximate_cfg_cache()
+        runner = OptimizedLatDitRunner(model, solver, device=dev)
+        ms = []
+        for seed in range(3):
+            inp = w.inputs(seed=100 + seed, device=dev)
+            runner.sample_with_context(inp["vox"], inp["context"], noise=inp["noise"])
+            torch.cuda.synchronize()
+            lat = None
+            for _ in range(reps):
+                flush.add_(1)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                lat = runner.sample_with_context(inp["vox"], inp["context"], noise=inp["noise"])
+                e1.record(s)
+                torch.cuda.synchronize()
+                ms.append(e0.elapsed_time(e1))
+            lats[(mode, seed)] = lat.float().cpu()
+        out[mode] = {"ms_per_sample": statistics.median(ms), "nfe_per_sample": 7 if mode == "exact" else 6}
+        del runner
+    errs = [float((lats[("neg_reuse", k)] - lats[("exact", k)]).norm() / lats[("exact", k)].norm()) for k in range(3)]
+    out["latent_rel_l2_vs_exact"] = errs
+    out["speedup"] = out["exact"]["ms_per_sample"] / out["neg_reuse"]["ms_per_sample"]
+    return out
+
+
 def kernel_table(timer: dict, hbm_peak: float, tensor_peak: float, peak_kind: str) -> list:
     """Per kernel class: launches, average CUDA-event duration, algorithmic FLOPs or bytes
     per launch and the fraction of the measured peak (sustained bf16 GEMM rate for
@@ -731,7 +773,7 @@ def main():
     ap.add_argument("--profile", action="store_true",
                     help="one warm-up sample, then one sample inside the NVTX range 'profile_step' (for ncu)")
     ap.add_argument("--only", choices=["attention", "dwconv", "dense_conv", "qknorm", "gate_add", "graph", "gemm", "branch_split",
-                                       "c5", "hbm"], default=None,
+                                       "c5", "hbm", "cfg_cache"], default=None,
                     help="run only one kernel on the workload's shapes (small ncu case); c5: the sharded batch")
     ap.add_argument("--samples", type=int, default=0, help="--only c5: batch size (default 16)")
     ap.add_argument("--c5-steps", type=int, default=1, help="timed passes of the C5 batch in the default run")
@@ -769,6 +811,9 @@ def main():
         flops, ms = attention_roofline(w, None)
         print(json.dumps({"kernel": "attention_kernel<128>", "ms_per_launch": ms, "tflops": flops / ms / 1e9,
                           "library": vendor_attention_bars(w)}))
+        return
+    if args.only == "cfg_cache":
+        print(json.dumps(cfg_cache_bench(w)))
         return
     if args.only == "qknorm":
         print(json.dumps(qknorm_bench(w)))

@@ -308,6 +308,24 @@ int vdit_gather_rows_f32(const float* src, const int64_t* idx, int64_t n, int32_
 int vdit_cfg_euler(float* xt, const float* v_pos, const float* v_neg, int64_t n, float guidance,
                    float dt, vdit_stream_t stream);
 
+/* Approximate CFG cache (opt-in; not part of the exact solver): one Euler step of a guided
+ * step that skips the unconditional NFE and reuses the last unconditional velocity, the
+ * reference's cfg_cache_mode "neg_reuse" (lib/fast_flow.py:2791-2887, non-QAOA branch).
+ * With zero_star: nc = last_neg, blended toward the clean endpoint (1 - a) * last_neg +
+ * a * (xt - last_neg_x0) / t_eval when last_neg_x0 is given and a = endpoint_blend > 0;
+ * s = clamp(<vp, nc> / max(<nc, nc>, 1e-6), 0.9, 1.1); delta = vp - s * nc;
+ * delta += hf_gain * (delta - row mean of delta).  Without it: delta = vp - last_neg.
+ * Then xt -= dt * (vp + guidance * delta).  xt, vp, last_neg, last_neg_x0: [n, 16] fp32;
+ * workspace of vdit_cfg_reuse_workspace_bytes() bytes (fixed-order reductions).
+ * vdit_neg_endpoint: x0 = xt - t_eval * v_neg at a step that ran the unconditional NFE. */
+size_t vdit_cfg_reuse_workspace_bytes(void);
+int vdit_cfg_reuse_euler(float* xt, const float* vp, const float* last_neg, const float* last_neg_x0,
+                         int64_t n, float guidance, float dt, float t_eval, float endpoint_blend,
+                         float hf_gain, int32_t zero_star, void* workspace, size_t workspace_bytes,
+                         vdit_stream_t stream);
+int vdit_neg_endpoint(const float* xt, const float* v_neg, int64_t n, float t_eval, float* x0,
+                      vdit_stream_t stream);
+
 /* out[i,:] = xt[up_widx[i],:] * scale + shift, 16 channels (unpermute +
  * denormalize, lib/fast_flow.py:3306-3313). */
 int vdit_unpermute_denorm(const float* xt, const int64_t* up_widx, int64_t n, const float* scale,

@@ -396,25 +396,68 @@ def build_schedule(num_steps: int = 4, n_guided: int = 3, rescale_t: float = 3.0
     return t, [True] * n_guided + [False] * n_unguided
 
 
+def cfg_reuse_delta(v_pos: torch.Tensor, last_neg: torch.Tensor, xt: torch.Tensor,
+                    last_neg_x0: Optional[torch.Tensor], t_eval: float, zero_star: bool = True,
+                    endpoint_blend: float = 0.08, hf_boost: float = 0.035, freq_decoupled: bool = True) -> torch.Tensor:
+    """The CFG delta of a guided step that reuses the last unconditional velocity
+    (``cfg_cache_mode`` "neg_reuse", ``lib/fast_flow.py:2844-2873``, non-QAOA branch): the
+    candidate is ``last_neg`` blended toward its clean endpoint while t > 0.25, projected with
+    CFG-Zero*'s clamped scale, then its per-channel row mean is used for the high-frequency boost."""
+    if not zero_star:
+        return v_pos - last_neg
+    cand = last_neg
+    if endpoint_blend > 0.0 and last_neg_x0 is not None and t_eval > 0.25:
+        cand = (1.0 - endpoint_blend) * last_neg + endpoint_blend * ((xt - last_neg_x0) * (1.0 / t_eval))
+    s = ((v_pos * cand).sum() / (cand * cand).sum().clamp_min(1e-6)).clamp(0.90, 1.10)
+    delta = v_pos - s * cand
+    if freq_decoupled and hf_boost > 0.0 and v_pos.shape[0] > 1:
+        dc = delta.mean(dim=0, keepdim=True)
+        delta = delta + hf_boost * max(0.0, 1.0 - t_eval) * (delta - dc)
+    return delta
+
+
+def should_eval_uncond(step: int, n_guided: int, cfg_stride: int, eval_uncond_steps) -> bool:
+    """``lib/fast_sampler.py:754-768`` for the "neg_reuse" mode."""
+    if eval_uncond_steps:
+        return step in eval_uncond_steps
+    if cfg_stride <= 1:
+        return True
+    if step == 0 or step == n_guided - 1:
+        return True
+    return step % cfg_stride == 0
+
+
 def sample(p: Params, cfg: ModelConfig, vox: np.ndarray, context: torch.Tensor, noise: torch.Tensor,
            guidance_scale: float = 3.0, num_steps: int = 4, n_guided: int = 3,
-           rescale_t: float = 3.0, cfg_range=(0.5, 1.0), one_token_uncond: bool = True):
+           rescale_t: float = 3.0, cfg_range=(0.5, 1.0), one_token_uncond: bool = True,
+           cfg_reuse: Optional[dict] = None):
     """Exact Euler + CFG sampler (``core.py:148-177`` update rule, fast-path
     schedule and unpermute/denormalize ``lib/fast_flow.py:2568-2576,
     2836, 3288, 3306-3313``).  ``noise`` is [N,16] in the caller's voxel
-    order; returns [N,16] latents in that order."""
+    order; returns [N,16] latents in that order.  ``cfg_reuse`` (a dict with
+    ``eval_uncond_steps``, ``cfg_stride`` and the ``cfg_reuse_delta`` options) switches on the
+    approximate CFG cache: guided steps it skips reuse the last unconditional velocity
+    (``lib/fast_flow.py:2791-2887``)."""
     geom = build_geometry(vox, cfg)
     xt = noise.float()[geom.perm]
     t_seq, guided = build_schedule(num_steps, n_guided, rescale_t, cfg_range)
     tl = t_seq.tolist()
+    last_neg = last_x0 = None
+    opts = dict(cfg_reuse or {})
+    steps, stride = opts.pop("eval_uncond_steps", [0, 2]), opts.pop("cfg_stride", 2)
     for i in range(num_steps):
         v = flow_forward(p, cfg, xt, tl[i], context, geom)
         if guided[i] and guidance_scale > 0:
-            if one_token_uncond:
-                vn = flow_forward_1tok(p, cfg, xt, tl[i], geom)
+            if cfg_reuse is None or last_neg is None or should_eval_uncond(i, n_guided, stride, steps):
+                if one_token_uncond:
+                    vn = flow_forward_1tok(p, cfg, xt, tl[i], geom)
+                else:
+                    vn = flow_forward(p, cfg, xt, tl[i], torch.zeros_like(context), geom)
+                if cfg_reuse is not None:
+                    last_neg, last_x0 = vn, xt - tl[i] * vn
+                v = v + guidance_scale * (v - vn)
             else:
-                vn = flow_forward(p, cfg, xt, tl[i], torch.zeros_like(context), geom)
-            v = v + guidance_scale * (v - vn)
+                v = v + guidance_scale * cfg_reuse_delta(v, last_neg, xt, last_x0, tl[i], **opts)
         xt = xt - (tl[i] - tl[i + 1]) * v
     out = xt[geom.up_widx]
     return (out * p["std"] + p["mean"]) * cfg.latent_scale

@@ -3,7 +3,7 @@
 Usage (needs the reference checkout, read-only; no GPU; the sampler case takes tens of
 minutes on a few host cores):
 
-    TORCHDYNAMO_DISABLE=1 python tests/golden/make_golden_full.py <reference-root> c1 c4nfe_128 c4nfe_96 c4sample
+    TORCHDYNAMO_DISABLE=1 python tests/golden/make_golden_full.py <reference-root> c1 c4nfe_128 c4nfe_96 c4sample cfgreuse
 
 Writes ``tests/golden/<case>.npz`` for each named case (``full_cases.CASES``):
 
@@ -18,6 +18,9 @@ Writes ``tests/golden/<case>.npz`` for each named case (``full_cases.CASES``):
   its cached 3D RoPE, ``lib/fast_kernels.py:1040-1075``, needs head_dim % 6 == 0.  Its exact
   schedule is the same: ``lib/fast_sampler.py:670-732`` with cfg_range (0.5, 1) gives three
   guided steps, as the baseline's ``cfg_range[0] <= t`` test does with cfg_range (0.6, 1).)
+
+``cfgreuse`` (-> ``cfg_reuse.npz``) pins the approximate CFG cache: the submission runner's
+``sample_fast`` in its "neg_reuse" mode on the small model of ``golden.npz``.
 
 Inputs and weights are rebuilt from seeds (``full_cases.py``), so only outputs and input
 checksums are stored.  ``BK/`` abbreviates ``baseline_repo/3dgen-main/``.
@@ -102,9 +105,51 @@ def sample_case(case: fc.Case) -> dict:
             "weight_checksum": np.array([wsum])}
 
 
+def cfg_reuse_case() -> dict:
+    """The submission runner's ``sample_fast`` (``lib/fast_flow.py:2523-3313``) with its approximate
+    CFG cache on: ``cfg_cache_mode`` "neg_reuse", ``cfg_stride`` 2, ``eval_uncond_steps`` [0, 2]
+    (its defaults, ``lib/fast_sampler.py:25-79``), QAOA and the context caches off, on the small
+    head_dim-96 model and inputs of ``golden.npz`` (``m96``, ``sample/*``)."""
+    from kandi3d_image23d.models.modeling_lat_dit import LatDitModel
+    from kandi3d_image23d.runtime import FlowMatchSamplingParams, LatDitConditioning
+    from lib.fast_flow import OptimizedLatDitRunner
+    from lib.fast_sampler import SolverConfig
+    from oracle import model as om
+
+    golden = dict(np.load(HERE / "golden.npz"))
+    cfg96 = om.ModelConfig(dim=192, head_dim=96, depth=3, cond_depth=1, res=64, patch_size=64)
+    mc = dict(res=64, latent_dim=16, dim=192, cond_depth=1, depth=3, head_dim=96, rms=True, rope=True,
+              pos_emb=False, ffn_conv=True, ffn_rate=2.5, patch=1, orders=["h", "ht1", "h1", "ht"],
+              patch_size=64, cfg=3.0, cfg_range=[0.5, 1.0], rescale_t=3.0)
+    model = LatDitModel(dim=192, latent_dim=16, latent_scale=1.5, cond=["image_last"], model_config=mc)
+    model.core.load_state_dict(om.init_params(cfg96, 11, weight_std=0.05, bias_std=0.02, scale_jitter=0.1),
+                               strict=True)
+    model.eval()
+    scfg = SolverConfig()
+    for k, v in dict(solver_type="piecewise_euler", qaoa_enabled=False, cfg_stride=2, cfg_cache_mode="neg_reuse",
+                     eval_uncond_steps=[0, 2], mid_block_cache_enabled=False, eval_cond_steps=[],
+                     guidance_scale=3.0, num_inference_steps=4, n_guided_steps=3, n_unguided_steps=1,
+                     cache_cond_block7_stride=1, uncond_mid_block_cache=False, warmup_on_load=False).items():
+        if hasattr(scfg, k):
+            setattr(scfg, k, v)
+    runner = OptimizedLatDitRunner(model, scfg)
+    dino = torch.from_numpy(golden["sample/dino"])[None]
+    with torch.no_grad():
+        lat = runner.sample_fast([torch.from_numpy(golden["m96/vox"])],
+                                 LatDitConditioning(dino_features=dino, batch_size=1),
+                                 sampling=FlowMatchSamplingParams(guidance_scale=3.0, cfg_range=(0.5, 1.0),
+                                                                  rescale_t=3.0, num_inference_steps=4),
+                                 generator=torch.Generator().manual_seed(1234))
+    return {"latents": lat[0].numpy()}
+
+
 def main(ref: Path, names) -> None:
     load_reference(ref)
     for name in names:
+        if name == "cfgreuse":
+            np.savez_compressed(HERE / "cfg_reuse.npz", **cfg_reuse_case())
+            print("wrote", HERE / "cfg_reuse.npz")
+            continue
         case = fc.CASES[name]
         out = sample_case(case) if name == "c4sample" else flow_case(case)
         out["meta"] = np.array([case.dim, case.head_dim, case.depth, case.cond_depth, case.n], dtype=np.int64)

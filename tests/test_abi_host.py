@@ -112,6 +112,21 @@ def test_solver_config_reads_json_and_ignores_approximations(tmp_path):
     assert "qaoa_enabled" in cfg.approximate_fields_ignored
 
 
+def test_solver_config_approximate_cfg_cache_is_opt_in(tmp_path):
+    """A config asking for the reference's CFG cache ("neg_reuse", stride 2, unconditional NFE at
+    guided steps 0 and 2) keeps the exact solver unless the caller opts in."""
+    (tmp_path / "solver_config.json").write_text(json.dumps(
+        {"cfg_cache_mode": "neg_reuse", "cfg_stride": 2, "eval_uncond_steps": [0, 2], "qaoa_enabled": True}))
+    exact = SolverConfig.from_dir(tmp_path)
+    assert not exact.approximate_cfg_cache and exact.cfg_stride == 1 and exact.eval_uncond_steps == []
+    assert {"cfg_cache_mode=neg_reuse", "cfg_stride=2", "eval_uncond_steps=[0, 2]"} <= set(exact.approximate_fields_ignored)
+    approx = SolverConfig.from_dir(tmp_path, allow_approximate_cfg_cache=True)
+    assert approx.approximate_cfg_cache and approx.cfg_stride == 2 and approx.eval_uncond_steps == [0, 2]
+    assert "qaoa_enabled" in approx.approximate_fields_ignored          # the QAOA solver is never taken
+    on = SolverConfig().enable_approximate_cfg_cache()
+    assert on.approximate_cfg_cache and on.eval_uncond_steps == [0, 2] and on.cfg_zero_star_projection
+
+
 def test_runtime_merge_and_generator_contract():
     base = FlowMatchSamplingParams(guidance_scale=7.0, num_inference_steps=4)
     r = resolve(base, FlowMatchSamplingParams(guidance_scale=3.0), cfg_range=[0.4, 1.0])

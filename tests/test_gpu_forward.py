@@ -6,6 +6,7 @@ import pytest
 import torch
 
 from vdit import _lib
+from vdit import fast_kernels as fk
 from vdit.fast_flow import OptimizedLatDitRunner
 from vdit.fast_sampler import SolverConfig
 from vdit.model import LatDitModel
@@ -102,6 +103,47 @@ def test_sampler_matches_oracle():
                              noise=noise.to(DEV))[0]
     assert lat.shape == (len(vox), 16) and lat.dtype == torch.float32
     assert rel(lat, lat_o) < 2e-2
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("zero_star,blend,hf,with_x0", [(True, 0.08, 0.02, True), (True, 0.08, 0.0, False),
+                                                       (False, 0.08, 0.02, True)])
+def test_cfg_reuse_step_matches_oracle(zero_star, blend, hf, with_x0):
+    """One Euler step of the approximate CFG cache (reuse of the last unconditional velocity)
+    against the oracle's restatement of the reference's formulas, fp32."""
+    n = 5000
+    g = torch.Generator().manual_seed(21)
+    xt, vp, ln, x0 = (torch.randn(n, 16, generator=g) for _ in range(4))
+    t_eval, dt, gs = 0.75, 0.25, 3.0
+    delta = om.cfg_reuse_delta(vp, ln, xt, x0 if with_x0 else None, t_eval, zero_star=zero_star,
+                               endpoint_blend=blend, hf_boost=hf / max(1e-9, 1.0 - t_eval) if hf else 0.0)
+    want = xt - dt * (vp + gs * delta)
+    got = xt.to(DEV).contiguous()
+    fk.cfg_reuse_euler_(got, vp.to(DEV), ln.to(DEV), x0.to(DEV) if with_x0 else None, gs, dt, t_eval, blend, hf,
+                        zero_star)
+    assert rel(got, want) < 1e-5
+    assert _lib.device_error() == 0
+
+
+def test_sampler_cfg_reuse_matches_reference(golden):
+    """The approximate sampler (unconditional NFE at guided steps 0 and 2, reused at step 1)
+    against the reference runner's ``sample_fast`` in its "neg_reuse" mode, on the small
+    head_dim-96 model of the golden fixtures (``tests/golden/cfg_reuse.npz``)."""
+    from pathlib import Path
+    fx = np.load(Path(__file__).resolve().parent / "golden" / "cfg_reuse.npz")
+    cfg = om.ModelConfig(dim=192, head_dim=96, depth=3, cond_depth=1, res=64, patch_size=64)
+    p = om.init_params(cfg, 11, weight_std=0.05, bias_std=0.02, scale_jitter=0.1)
+    mc = {"dim": 192, "head_dim": 96, "depth": 3, "cond_depth": 1, "res": 64, "patch_size": 64,
+          "latent_scale": cfg.latent_scale}
+    solver = SolverConfig(guidance_scale=3.0).enable_approximate_cfg_cache()
+    runner = OptimizedLatDitRunner(LatDitModel.from_state_dict(p, mc), solver, device=torch.device(DEV))
+    dino = torch.from_numpy(golden["sample/dino"])[None]
+    lat = runner.sample_fast([torch.from_numpy(golden["m96/vox"]).to(DEV)],
+                             LatDitConditioning(dino_features=dino.to(DEV)),
+                             noise=torch.from_numpy(golden["sample/noise"]).to(DEV))[0]
+    err = rel(lat, torch.from_numpy(fx["latents"]))
+    print(f"\ncfg reuse sampler: rel L2 vs the reference's approximate sampler {err:.3e}")
+    assert err < 2e-2
     assert _lib.device_error() == 0
 
 

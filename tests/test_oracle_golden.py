@@ -110,6 +110,20 @@ def test_sampler_matches_reference(golden):
     assert _rel(lat, torch.from_numpy(golden["sample/latents"])) < 1e-5
 
 
+def test_cfg_reuse_sampler_matches_reference(golden):
+    """The approximate CFG cache ("neg_reuse": the unconditional NFE at guided steps 0 and 2,
+    reused with the CFG-Zero* projection, clean-endpoint blend and high-frequency boost at step
+    1) against the reference runner's own ``sample_fast`` in that mode (``cfg_reuse.npz``)."""
+    from pathlib import Path
+    fx = np.load(Path(__file__).resolve().parent / "golden" / "cfg_reuse.npz")
+    cfg, p, geom = _model(golden, "m96")
+    dino = torch.from_numpy(golden["sample/dino"])
+    ctx = torch.nn.functional.linear(dino, p["image_map.weight"], p["image_map.bias"])
+    lat = om.sample(p, cfg, golden["m96/vox"], ctx, torch.from_numpy(golden["sample/noise"]),
+                    guidance_scale=3.0, num_steps=4, n_guided=3, cfg_reuse={})
+    assert _rel(lat, torch.from_numpy(fx["latents"])) < 1e-5
+
+
 def test_schedule():
     t, guided = om.build_schedule(4, 3, 3.0, (0.5, 1.0))
     assert np.allclose(t.numpy(), [1.0, 0.9, 0.75, 0.5, 0.0], atol=1e-6)
