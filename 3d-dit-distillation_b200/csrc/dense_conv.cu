@@ -9,7 +9,11 @@
 // lanes per row, 16-byte copies into the 128B-swizzled K-major layout the MMA reads;
 // absent neighbours copy zero bytes and read as zeros), warp 8 loads the weight
 // tile W[d, co0:co0+256, k0:k0+64] with TMA (128B swizzle), warp 9 issues the
-// MMAs.  A 3-stage ring overlaps gathers, weight loads and MMAs.  Taps that no
+// MMAs.  A 3-stage ring overlaps gathers, weight loads and MMAs: a gather thread
+// marks stage i full as soon as its copies for stage i have landed (checked after it
+// issued stage i+1), so the MMAs of two stages can be queued on the tensor core while
+// the next gather is in flight (marking stage i only after issuing stage i+2 waited
+// for the MMAs of stage i-1 and left the tensor core idle at every hand-off).  Taps that no
 // row of the CTA has are skipped.  Warps 0..7 then drain TMEM (warp w: tile
 // w/4, lane quarter w%4), add the bias and store bf16.  All mbarrier waits are
 // bounded (error word + CTA abort flag).
@@ -134,15 +138,15 @@ __global__ void __launch_bounds__(THREADS, 1) dense_conv27_kernel(const __grid_c
                 cp_async16(smem_u32(sm.a[s][rr / BM]) + rt * 128 + ((ch ^ (rt & 7)) << 4), p, src >= 0 ? 16u : 0u);
             }
             asm volatile("cp.async.commit_group;" ::: "memory");
-            if (i >= S - 1) {
-                asm volatile("cp.async.wait_group %0;" ::"n"(S - 1) : "memory");
+            if (i >= 1) {   // stage i-1 is complete once at most this stage's group is pending
+                asm volatile("cp.async.wait_group 1;" ::: "memory");
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive(smem_u32(&sm.full_a[(i - (S - 1)) % S]));
+                mbar_arrive(smem_u32(&sm.full_a[(i - 1) % S]));
             }
         }
         asm volatile("cp.async.wait_group 0;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        for (int j = max(0, i - (S - 1)); j < i; ++j) mbar_arrive(smem_u32(&sm.full_a[j % S]));
+        for (int j = max(0, i - 1); j < i; ++j) mbar_arrive(smem_u32(&sm.full_a[j % S]));
         // ------------------------------------------------------------ epilogue
         const bool ok = __all_sync(0xffffffffu, i == n_iter &&
                                                     mbar_wait(smem_u32(&sm.acc_full), 0, abort_flag, &g_dense_error, kErr));
