@@ -27,7 +27,7 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompil
 
 
 # per-file extra flags: the attention kernel keeps a 128-column score row in
-# registers per thread (320 threads, one CTA per SM), so it may use up to 200.
+# registers per thread (224 threads, one CTA per SM), so it may use up to 200.
 EXTRA = {"attention.cu": ["-maxrregcount=200"]}
 
 
