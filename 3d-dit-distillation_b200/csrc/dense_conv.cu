@@ -184,30 +184,34 @@ __global__ void __launch_bounds__(THREADS, 1) dense_conv27_kernel(const __grid_c
         }
     } else {
         // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t IDESC = make_idesc(BM, BN, false);
-            bool ok = true;
-            for (int i = 0; i < n_iter; ++i) {
-                const int s = i % S;
-                if (!mbar_wait(smem_u32(&sm.full_a[s]), (i / S) & 1, abort_flag, &g_dense_error, kErr) ||
-                    !mbar_wait(smem_u32(&sm.full_b[s]), (i / S) & 1, abort_flag, &g_dense_error, kErr)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t bbase = smem_u32(sm.b[s]);
-#pragma unroll
-                for (int t = 0; t < MT; ++t) {
-                    const uint32_t abase = smem_u32(sm.a[s][t]);
-#pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk)
-                        tc_mma(tmem + t * BN, make_desc(abase + kk * 32, 16, 1024, kSw128),
-                               make_desc(bbase + kk * 32, 16, 1024, kSw128), IDESC, (i > 0 || kk > 0) ? 1u : 0u);
-                }
-                tc_commit(smem_u32(&sm.empty[s]));
+        // the whole warp runs the loop (every lane waits, the elected lane issues), with the
+        // descriptors as per-CTA bases plus stage, tile and k offsets (uniform registers)
+        constexpr uint32_t IDESC = make_idesc(BM, BN, false);
+        const uint64_t ad0 = make_desc(smem_u32(sm.a[0][0]), 16, 1024, kSw128);
+        const uint64_t bd0 = make_desc(smem_u32(sm.b[0]), 16, 1024, kSw128);
+        auto wait = [&](uint32_t bar, uint32_t parity) {
+            return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, &g_dense_error, kErr));
+        };
+        bool ok = true;
+        for (int i = 0; i < n_iter; ++i) {
+            const int s = i % S;
+            if (!wait(smem_u32(&sm.full_a[s]), (i / S) & 1) || !wait(smem_u32(&sm.full_b[s]), (i / S) & 1)) {
+                ok = false;
+                break;
             }
-            if (ok) tc_commit(smem_u32(&sm.acc_full));
+            tc_fence_after();
+            const uint64_t bd = bd0 + (uint64_t)(s * (int)(sizeof(sm.b[0]) >> 4));
+#pragma unroll
+            for (int t = 0; t < MT; ++t) {
+                const uint64_t ad = ad0 + (uint64_t)(s * (int)(sizeof(sm.a[0]) >> 4) + t * (int)(sizeof(sm.a[0][0]) >> 4));
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk)
+                    tc_mma_elect(tmem + t * BN, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), IDESC,
+                                 (i > 0 || kk > 0) ? 1u : 0u);
+            }
+            tc_commit_elect(smem_u32(&sm.empty[s]));
         }
+        if (ok) tc_commit_elect(smem_u32(&sm.acc_full));
     }
 
     tc_fence_before();

@@ -180,32 +180,38 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer (even CTA)
-        if (leader && lane == 0) {
+        // the whole warp runs the loop (every lane waits, the elected lane issues), with the
+        // descriptors as per-CTA bases plus stage and k offsets, so they stay in uniform registers
+        if (leader) {
             constexpr uint32_t IDESC = make_idesc(2 * BM, BN, false);
+            const uint64_t ad0 = make_desc(smem_u32(sm.a[0]), 16, 1024, kSw128);
+            const uint64_t bd0 = make_desc(smem_u32(sm.b[0]), 16, 1024, kSw128);
+            auto wait = [&](uint32_t bar, uint32_t parity) {
+                return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, &g_gemm_error, kErr));
+            };
             int it = 0, lt = 0;
             bool ok = true;
             for (int t = pair; ok && t < ntiles; t += npairs, ++lt) {
                 const int buf = lt & 1;
-                if (lt >= 2 && !mbar_wait(smem_u32(&sm.acc_empty[buf]), ((lt >> 1) - 1) & 1, abort_flag,
-                                          &g_gemm_error, kErr))
-                    break;
+                if (lt >= 2 && !wait(smem_u32(&sm.acc_empty[buf]), ((lt >> 1) - 1) & 1)) break;
                 tc_fence_after();
                 const uint32_t acc = tmem + buf * BN;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int s = it % STAGES;
-                    if (!mbar_wait(smem_u32(&sm.full[s]), (it / STAGES) & 1, abort_flag, &g_gemm_error, kErr)) {
+                    if (!wait(smem_u32(&sm.full[s]), (it / STAGES) & 1)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t abase = smem_u32(sm.a[s]), bbase = smem_u32(sm.b[s]);
+                    const uint64_t ad = ad0 + (uint64_t)(s * (int)(sizeof(sm.a[0]) >> 4));
+                    const uint64_t bd = bd0 + (uint64_t)(s * (int)(sizeof(sm.b[0]) >> 4));
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk)
-                        tc_mma_pair(acc, make_desc(abase + kk * 32, 16, 1024, kSw128),
-                                    make_desc(bbase + kk * 32, 16, 1024, kSw128), IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
-                    tc_commit_pair(smem_u32(&sm.empty[s]), 0x3);
+                        tc_mma_pair_elect(acc, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), IDESC,
+                                          (kb > 0 || kk > 0) ? 1u : 0u);
+                    tc_commit_pair_elect(smem_u32(&sm.empty[s]), 0x3);
                 }
-                if (ok) tc_commit_pair(smem_u32(&sm.acc_full[buf]), 0x3);
+                if (ok) tc_commit_pair_elect(smem_u32(&sm.acc_full[buf]), 0x3);
             }
         }
     } else {

@@ -305,6 +305,28 @@ __device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t a_desc, ui
         : "memory");
 }
 
+// tc_mma_pair issued by the elected lane of a converged warp (see tc_mma_elect)
+__device__ __forceinline__ void tc_mma_pair_elect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                  uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
+// tc_commit_pair by the elected lane (the lane that issued the MMAs of tc_mma_pair_elect)
+__device__ __forceinline__ void tc_commit_pair_elect(uint32_t bar, uint16_t cta_mask) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}"
+        ::"r"(bar), "h"(cta_mask)
+        : "memory");
+}
+
 // completion of this thread's earlier pair MMAs arrives once on the mbarrier at the same
 // shared-memory offset in every CTA of `cta_mask`
 __device__ __forceinline__ void tc_commit_pair(uint32_t bar, uint16_t cta_mask) {
