@@ -724,26 +724,37 @@ def cfg_cache_bench(w, reps: int = 5) -> dict:
     return out
 
 
-def kernel_table(timer: dict, hbm_peak: float, tensor_peak: float, peak_kind: str) -> list:
+def kernel_table(timer: dict, hbm_peak: float, tensor_peak: float, peak_kind: str, solo: dict = None) -> list:
     """Per kernel class: launches, average CUDA-event duration, algorithmic FLOPs or bytes
     per launch and the fraction of the measured peak (sustained bf16 GEMM rate for
-    tensor-core classes, HBM copy bandwidth for byte-bound ones)."""
+    tensor-core classes, HBM copy bandwidth for byte-bound ones).  `timer` holds the launches
+    inside the timed steps, where a guided step runs its two NFEs on two streams that share
+    the GPU; `solo`, when given, the same classes from one NFE of each branch run by itself
+    (`solo_ms_per_launch`, `solo_frac`; the NFE's own context stream still overlaps its voxel
+    stream in the context blocks)."""
     from vdit.fast_flow import KERNEL_CLASSES
-    rows = []
-    for kind, ev in timer.items():
-        if not ev:
-            continue
+
+    def rate(kind, ev):
         ms = statistics.fmean(a.elapsed_time(b) for a, b, _, _ in ev)
         units = statistics.fmean(u for _, _, u, _ in ev)
         bound = KERNEL_CLASSES.get(kind, "tensor")
         if bound == "tensor":
-            ach, unit, peak = units / (ms / 1e3) / 1e12, "TFLOP/s", tensor_peak
-        else:
-            ach, unit, peak = units / (ms / 1e3) / 1e9, "GB/s", hbm_peak
-        rows.append({"kernel": kind, "bound": bound, "launches": len(ev), "ms_per_launch": ms,
-                     "units_per_launch": units, "achieved": ach, "unit": unit, "peak": peak, "frac": ach / peak,
-                     "total_ms": ms * len(ev),
-                     "peak_kind": f"{peak_kind} {'sustained bf16' if bound == 'tensor' else 'HBM copy'}"})
+            return bound, ms, units, units / (ms / 1e3) / 1e12, "TFLOP/s", tensor_peak
+        return bound, ms, units, units / (ms / 1e3) / 1e9, "GB/s", hbm_peak
+
+    rows = []
+    for kind, ev in timer.items():
+        if not ev:
+            continue
+        bound, ms, units, ach, unit, peak = rate(kind, ev)
+        row = {"kernel": kind, "bound": bound, "launches": len(ev), "ms_per_launch": ms,
+               "units_per_launch": units, "achieved": ach, "unit": unit, "peak": peak, "frac": ach / peak,
+               "total_ms": ms * len(ev),
+               "peak_kind": f"{peak_kind} {'sustained bf16' if bound == 'tensor' else 'HBM copy'}"}
+        if solo and solo.get(kind):
+            _, sms, _, sach, _, _ = rate(kind, solo[kind])
+            row.update(solo_ms_per_launch=sms, solo_achieved=sach, solo_frac=sach / peak)
+        rows.append(row)
     rows.sort(key=lambda r: -r["total_ms"])
     return rows
 
@@ -916,6 +927,16 @@ def main():
         e1.record(s)
         torch.cuda.synchronize()
         nfe[name] = {"ms": e0.elapsed_time(e1) / 3, "voxel_tokens_per_s": w.n / (e0.elapsed_time(e1) / 3e3)}
+    # the kernel classes of one NFE of each branch, each NFE alone on the GPU
+    ksolo: dict = {}
+    for name, kw in (("pos", {}), ("neg_1tok", {"uncond": True})):
+        if name == "neg_1tok":
+            runner._b0_share = None
+        _l2_flush(flush)
+        runner.kernel_timer = ksolo
+        runner.forward_flow_fast(xs, 0.9, inp["context"], None, geom, **kw)
+        runner.kernel_timer = None
+    torch.cuda.synchronize()
 
     # ---------------------------------------------------------------- e2e through the plugin API
     vox_h = inp["vox_host"].pin_memory()
@@ -959,7 +980,7 @@ def main():
     solo_ms = statistics.fmean(a.elapsed_time(b) for a, b in solo) if solo else None
     flops_alone, att_ms_alone = attention_roofline(w, runner)
     traffic = attention_traffic()
-    kernels = kernel_table(ktimer, hbm, tflops_sustained, peak_kind)
+    kernels = kernel_table(ktimer, hbm, tflops_sustained, peak_kind, solo=ksolo)
     assert _lib.device_error() == 0, "device error word set during the benchmark"
 
     # ---------------------------------------------------------------- C5 sharded batch (strong scaling)
