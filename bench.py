@@ -729,9 +729,8 @@ def kernel_table(timer: dict, hbm_peak: float, tensor_peak: float, peak_kind: st
     per launch and the fraction of the measured peak (sustained bf16 GEMM rate for
     tensor-core classes, HBM copy bandwidth for byte-bound ones).  `timer` holds the launches
     inside the timed steps, where a guided step runs its two NFEs on two streams that share
-    the GPU; `solo`, when given, the same classes from one NFE of each branch run by itself
-    (`solo_ms_per_launch`, `solo_frac`; the NFE's own context stream still overlaps its voxel
-    stream in the context blocks)."""
+    the GPU; `solo`, when given, the same classes from one NFE of each branch with every kernel
+    alone on the GPU (`solo_ms_per_launch`, `solo_frac`)."""
     from vdit.fast_flow import KERNEL_CLASSES
 
     def rate(kind, ev):
@@ -927,8 +926,11 @@ def main():
         e1.record(s)
         torch.cuda.synchronize()
         nfe[name] = {"ms": e0.elapsed_time(e1) / 3, "voxel_tokens_per_s": w.n / (e0.elapsed_time(e1) / 3e3)}
-    # the kernel classes of one NFE of each branch, each NFE alone on the GPU
+    # the kernel classes of one NFE of each branch with every kernel alone on the GPU: one NFE at
+    # a time and its context-stream work on the voxel stream (no overlap inside the NFE either)
     ksolo: dict = {}
+    overlap = runner.overlap_context
+    runner.overlap_context = False
     for name, kw in (("pos", {}), ("neg_1tok", {"uncond": True})):
         if name == "neg_1tok":
             runner._b0_share = None
@@ -937,6 +939,7 @@ def main():
         runner.forward_flow_fast(xs, 0.9, inp["context"], None, geom, **kw)
         runner.kernel_timer = None
     torch.cuda.synchronize()
+    runner.overlap_context = overlap
 
     # ---------------------------------------------------------------- e2e through the plugin API
     vox_h = inp["vox_host"].pin_memory()
