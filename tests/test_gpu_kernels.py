@@ -363,6 +363,21 @@ def test_attention_matches_fp32(heads, hd, cu_q, cu_k):
     assert rel(out, ref) < 1e-2
 
 
+@pytest.mark.parametrize("heads,hd", [(12, 128), (16, 96)])
+def test_attention_empty_key_segment_gives_zeros(heads, hd):
+    """A segment with queries and no keys writes zero rows; the segments around it are unaffected
+    (a query tile of the empty segment shares no barrier with them)."""
+    cu_q, cu_k = [0, 130, 330, 331], [0, 0, 257, 600]
+    g = torch.Generator(device=DEV).manual_seed(91 + hd)
+    D = heads * hd
+    q = torch.randn(cu_q[-1], D, device=DEV, generator=g).to(torch.bfloat16)
+    kv = torch.randn(cu_k[-1], 2 * D, device=DEV, generator=g).to(torch.bfloat16)
+    out = fk.attention(q, kv[:, :D], kv[:, D:], cu_q, cu_k, heads, hd)
+    assert torch.count_nonzero(out[:130]) == 0
+    ref = ref_attention(q[130:], kv[:, :D], kv[:, D:], [0, 200, 201], [0, 257, 600], heads, hd)
+    assert rel(out[130:], ref) < 1e-2
+
+
 def test_attention_scatter_and_large_logits():
     heads, hd, n = 12, 128, 4096 + 700
     g = torch.Generator(device=DEV).manual_seed(1)
