@@ -35,6 +35,8 @@ SIGNATURES = {
     "vdit_gate_add_modulate": (ctypes.c_int, [_vp, _vp, _c_i64, _c_i64, _c_i32, _vp, _vp, _vp, _vp, _vp]),
     "vdit_gate_add2_modulate": (ctypes.c_int, [_vp, _vp, _c_i64, _c_i64, _c_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "vdit_out_modulate_unpatchify": (ctypes.c_int, [_vp, _c_i64, _c_i32, _vp, _vp, _vp, _vp, _vp]),
+    "vdit_unpatchify_project": (ctypes.c_int, [_vp, _c_i64, _c_i32, _vp, _vp, _vp]),
+    "vdit_split_weight3": (ctypes.c_int, [_vp, _c_i32, _c_i32, _vp, _vp]),
     "vdit_qknorm_rope3d_gather": (ctypes.c_int, [_vp, _c_i64, _c_i32, _c_i32, _vp, _vp, _vp, _vp, _c_i32, _vp,
                                                  _vp, _vp, _vp]),
     "vdit_qknorm_rope2d": (ctypes.c_int, [_vp, _c_i64, _c_i32, _c_i32, _vp, _vp, _vp, _vp, _c_i32, _vp]),

@@ -480,6 +480,7 @@ int dense_conv_error_word(int clear);   // error word of the dense conv kernel (
 int dwconv_plan_error_word(int clear);  // error word of the staged depthwise conv (dwconv_plan.cu)
 int rowops_error_word(int clear);       // error word of the staged row kernels (rowops.cu)
 int gemm_error_word(int clear);         // error word of the tcgen05 GEMM (gemm.cu)
+int unpatch_error_word(int clear);      // error word of the unpatchify projection (unpatchify.cu)
 }
 
 extern "C" int vdit_device_error(int clear) {
@@ -498,5 +499,7 @@ extern "C" int vdit_device_error(int clear) {
     if (r < 0) return r;
     const int g = vdit::gemm_error_word(clear);
     if (g < 0) return g;
-    return v != 0 ? v : (d != 0 ? d : (p != 0 ? p : (r != 0 ? r : g)));
+    const int u = vdit::unpatch_error_word(clear);
+    if (u < 0) return u;
+    return v != 0 ? v : (d != 0 ? d : (p != 0 ? p : (r != 0 ? r : (g != 0 ? g : u))));
 }

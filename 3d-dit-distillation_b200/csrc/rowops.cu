@@ -138,7 +138,9 @@ __global__ void __launch_bounds__(256) gate_add_modulate_kernel(
 // per SM stages g, s1, sh in shared memory once, and each warp walks rows with
 // a stride, bulk-copying the next row's x and h into its second buffer while
 // the current row is reduced and written.  With h == nullptr the kernel is the
-// plain modulation (modulate_kernel): only x is copied and x is not written.
+// plain modulation (modulate_kernel): only x is copied, into a four-row ring
+// (three rows in flight per warp, the same bytes in flight as with the
+// residual), and x is not written.
 // Arithmetic is identical to the one-row-per-warp kernels.  Waits on the bulk
 // copies are bounded; a timeout sets the row kernels' error word.
 constexpr int kGaMaxWarps = 16;
@@ -167,10 +169,12 @@ __global__ void __launch_bounds__(kGaMaxWarps * 32, 1) gate_add_modulate_staged_
     float* pg2 = psh + d;            // second residual: its gate and its (broadcast) row in fp32
     float* pc2 = pg2 + d;
     const uint32_t row_bytes = 2u * (uint32_t)d;
-    uint8_t* wbuf = smem + (size_t)kGaVecBytes * d + (size_t)warp * 4 * row_bytes;   // [stage][x | h]
+    // a warp's four row slots: two stages of [x | h] with the residual, else four stages of x
+    const int nst = add ? 2 : 4;
+    uint8_t* wbuf = smem + (size_t)kGaVecBytes * d + (size_t)warp * 4 * row_bytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kGaVecBytes * d + (size_t)nwarps * 4 * row_bytes) +
-                     warp * 2;
-    const uint32_t bar_u[2] = {tc::smem_u32(bars), tc::smem_u32(bars + 1)};
+                     warp * 4;
+    const uint32_t bar0 = tc::smem_u32(bars);
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
         if (add) pg[i] = g[i];
         if (mod) {
@@ -184,31 +188,34 @@ __global__ void __launch_bounds__(kGaMaxWarps * 32, 1) gate_add_modulate_staged_
     }
     if (threadIdx.x == 0) abort_flag = 0;
     if (lane == 0) {
-        tc::mbar_init(bar_u[0], 1);
-        tc::mbar_init(bar_u[1], 1);
+        for (int b = 0; b < nst; ++b) tc::mbar_init(bar0 + 8 * b, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
 
     const int nvec = d >> 3;
     const int64_t stride = (int64_t)gridDim.x * nwarps;
+    const int slot_rows = add ? 2 : 1;
     auto issue = [&](int64_t row, int b) {
-        const uint32_t dst = tc::smem_u32(wbuf + b * 2 * row_bytes);
-        tc::mbar_expect_tx(bar_u[b], (add ? 2 : 1) * row_bytes);
-        bulk_load(dst, x + row * d, row_bytes, bar_u[b]);
-        if (add) bulk_load(dst + row_bytes, h + row * h_stride, row_bytes, bar_u[b]);
+        const uint32_t dst = tc::smem_u32(wbuf + b * slot_rows * row_bytes);
+        tc::mbar_expect_tx(bar0 + 8 * b, slot_rows * row_bytes);
+        bulk_load(dst, x + row * d, row_bytes, bar0 + 8 * b);
+        if (add) bulk_load(dst + row_bytes, h + row * h_stride, row_bytes, bar0 + 8 * b);
     };
     int64_t row = (int64_t)blockIdx.x * nwarps + warp;
-    if (lane == 0 && row < m) issue(row, 0);
+    if (lane == 0)
+        for (int k = 0; k < nst - 1; ++k)
+            if (row + k * stride < m) issue(row + k * stride, k);
     int it = 0;
     bool ok = true;
     for (; row < m; row += stride, ++it) {
-        const int b = it & 1;
-        if (lane == 0 && row + stride < m) issue(row + stride, b ^ 1);   // its buffer was read last row
-        ok = __all_sync(0xffffffffu, tc::mbar_wait(bar_u[b], (it >> 1) & 1, &abort_flag, &g_rowops_error,
+        const int b = it % nst;
+        // the row nst - 1 ahead goes into the buffer read in the previous iteration
+        if (lane == 0 && row + (nst - 1) * stride < m) issue(row + (nst - 1) * stride, (it + nst - 1) % nst);
+        ok = __all_sync(0xffffffffu, tc::mbar_wait(bar0 + 8 * b, (it / nst) & 1, &abort_flag, &g_rowops_error,
                                                    kErrRowTimeout));
         if (!ok) break;
-        const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(wbuf + b * 2 * row_bytes);
+        const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(wbuf + b * slot_rows * row_bytes);
         const __nv_bfloat16* hs = xs + d;
         __nv_bfloat16* xr = x + row * d;
         RowRegs r;
@@ -274,136 +281,301 @@ __global__ void __launch_bounds__(kGaMaxWarps * 32, 1) gate_add_modulate_staged_
         }
     }
     if (lane == 0 && !ok) {
-        // a wait ran out: give the copies still in flight (rows it and it+1) time to land
+        // a wait ran out: give the copies still in flight (rows it .. it + nst - 1) time to land
         volatile int no_abort = 0;
-        int ignored = 0;
-        for (int k = it; k < it + 2; ++k) tc::mbar_wait(bar_u[k & 1], (k >> 1) & 1, &no_abort, &ignored, 0);
+        for (int k = it; k < it + nst; ++k)
+            if (row + (k - it) * stride < m)
+                tc::mbar_wait(bar0 + 8 * (k % nst), (k / nst) & 1, &no_abort, &g_rowops_error, kErrRowTimeout);
     }
 }
 
-// out[row, o] = sum_c bf16(LN(x)*s1+sh)[c] * w[o, c], 16 outputs, fp32.  The weight
-// (16 x d fp32) is staged in shared memory once per CTA, split so that the lanes'
-// 16-byte reads are consecutive (no bank conflicts): float4 slot (2o + h) * nvec + vi
-// holds w[o, 8vi + 4h .. 8vi + 4h + 3].  A warp takes two rows at a time, so one pass over
-// the weight serves both; lane l holds channels 8(l + 32i) .. +7 of each row.  The 2 x 16
-// per-lane partial sums are reduced by a butterfly that halves the values a lane keeps at
-// every step (the additions pair up as in warp_sum), leaving output o of row k of the pair
-// in lane 16k + o, so the two rows' 32 outputs leave in one 128-byte store.
-constexpr int kUnpRows = 2;
-constexpr int kUnpWarps = 8;
+// out[row, o] = sum_c y[row, c] * w[o, c] with y = bf16(LN(x[row]) * s1 + sh) and fp32 weights
+// w [16, d]: 16 fp32 outputs per row, on the tensor cores at fp32 accuracy.  Each weight is split
+// into three bf16 parts, hi = bf16(w), mid = bf16(w - hi), lo = bf16(w - hi - mid): both
+// differences are exact in fp32 and hi + mid + lo carries w's 24-bit significand.  B = [hi; mid;
+// lo] is then a 48 x d bf16 matrix, every product y * part (bf16 x bf16) is exact in the fp32
+// accumulator, and one M=128, N=48 MMA chain gives the three partial sums of each output, which
+// the epilogue adds (lo + mid first).
+// A CTA takes 128 rows.  Phase 1: warps 0-7 compute the rows' LayerNorm statistics with the sums
+// of row_stats (16 rows per warp), the one HBM read of x: each warp streams its rows through a
+// ring of up to six row slots filled by bulk copies (the stage buffers, idle until phase 2), so
+// five rows stay in flight while one is reduced.  Phase 2: per 64-column chunk the warps read the
+// chunk again (from L2), modulate it into a 128-row x 128-byte stage in the 128-byte-swizzled
+// K-major layout of the MMA's A operand (16-byte piece c of row r at (r / 8) * 1024 + (r % 8) *
+// 128 + ((c ^ r % 8) * 16)), and write the chunk's split weights into the stage's B part in the
+// same layout; four chunks are prepared per round, their row and weight loads issued together,
+// each chunk on its own stage of an eight-stage ring, with s1 and sh read from shared memory.
+// Warp 8 issues each chunk's four K=16 MMAs and frees the stage with a commit.  Warps 0-3 read the
+// 128 x 48 accumulator back from TMEM and store the 16 outputs of a row.
+constexpr int kUpRows = 128;                                   // rows per CTA (the MMA's M)
+constexpr int kUpK = 64;                                       // columns per chunk (128 bytes of bf16)
+constexpr int kUpN = 48;                                       // hi, mid and lo parts of 16 outputs
+constexpr int kUpStages = 8;
+constexpr int kUpRound = 4;                                    // chunks prepared per round
+constexpr int kUpWarps = 8;                                    // + warp 8, the MMA issuer
+constexpr int kUpSlots = 6;                                    // phase-1 row slots per warp (at most)
+constexpr int kUpMaxD = 256 * kMaxVec;
+constexpr int kUpABytes = kUpRows * 128;
+constexpr int kUpStageBytes = kUpABytes + kUpN * 128;          // 22 KB, a multiple of 1024
+constexpr int kUpBarOff = kUpStages * kUpStageBytes;           // phase-2 barriers, TMEM slot, abort flag
+constexpr int kUpRowBarOff = kUpBarOff + 256;                  // phase-1 slot barriers
+constexpr int kUpStatsOff = kUpRowBarOff + kUpWarps * kUpSlots * 8;
+constexpr int kUpVecOff = kUpStatsOff + kUpRows * 8;           // s1, sh as fp32
+constexpr int kUpSmem = 1024 + kUpVecOff + 2 * kUpMaxD * 4;    // 1024: alignment slack
+constexpr int kErrUnpTimeout = 0x5550;                         // "UP": a bounded wait ran out
+static_assert(kUpStageBytes % 1024 == 0 && kUpStages % kUpRound == 0, "stage layout");
+static_assert((2 * kUpStages + 1) * 8 + 8 <= 256, "barrier area");
+static_assert(kUpSmem <= 227 * 1024, "shared memory per CTA");
 
-__global__ void __launch_bounds__(kUnpWarps * 32) out_unpatchify_kernel(
+__device__ __forceinline__ uint32_t up_swz(int r, int c) {      // byte offset of 16-byte piece c of row r
+    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// VEC: 16-byte vectors per lane of a row in phase 1 (d <= 256 VEC)
+template <int VEC>
+__global__ void __launch_bounds__((kUpWarps + 1) * 32, 1) out_unpatchify_kernel(
         const __nv_bfloat16* __restrict__ x, int64_t m, int d, const float* __restrict__ s1,
         const float* __restrict__ sh, const float* __restrict__ w, float* __restrict__ out) {
-    extern __shared__ float4 w_s[];
+    using namespace tc;
+    extern __shared__ uint8_t up_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(up_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kUpBarOff);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kUpStages + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float2* stats = reinterpret_cast<float2*>(sm + kUpStatsOff);
+    float* s1_s = reinterpret_cast<float*>(sm + kUpVecOff);
+    float* sh_s = s1_s + kUpMaxD;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nvec = d >> 3, d4 = d >> 2;
-    // staging: each thread issues a batch of loads before it stores any of them
-    constexpr int kStageBatch = 12;
-    for (int q0 = tid; q0 < 16 * d4; q0 += kUnpWarps * 32 * kStageBatch) {
-        float4 t[kStageBatch];
-#pragma unroll
-        for (int b = 0; b < kStageBatch; ++b) {
-            const int q = q0 + b * kUnpWarps * 32;
-            if (q < 16 * d4) t[b] = __ldg(reinterpret_cast<const float4*>(w) + q);
+    const int64_t row0 = (int64_t)blockIdx.x * kUpRows;
+    const int nvec = d >> 3;
+    const int nk = (d + kUpK - 1) / kUpK;
+    const uint32_t row_bytes = 2u * (uint32_t)d;
+    const int nslot = min(kUpSlots, kUpBarOff / (kUpWarps * (int)row_bytes));
+    auto full = [&](int s) { return smem_u32(&bars[s]); };
+    auto empty = [&](int s) { return smem_u32(&bars[kUpStages + s]); };
+    const uint32_t done = smem_u32(&bars[2 * kUpStages]);
+    const uint32_t rbar0 = smem_u32(sm + kUpRowBarOff) + warp * kUpSlots * 8;
+
+    if (tid == 0) {
+        for (int s = 0; s < kUpStages; ++s) {
+            mbar_init(full(s), kUpWarps);
+            mbar_init(empty(s), 1);
         }
-#pragma unroll
-        for (int b = 0; b < kStageBatch; ++b) {
-            const int q = q0 + b * kUnpWarps * 32;
-            if (q >= 16 * d4) break;
-            const int o = q / d4, c4 = q - o * d4;
-            w_s[(o * 2 + (c4 & 1)) * nvec + (c4 >> 1)] = t[b];
-        }
+        mbar_init(done, 1);
+        for (int k = 0; k < kUpWarps * kUpSlots; ++k) mbar_init(smem_u32(sm + kUpRowBarOff) + 8 * k, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    for (int i = tid; i < d; i += blockDim.x) {
+        s1_s[i] = s1[i];
+        sh_s[i] = sh[i];
     }
     __syncthreads();
-    const int64_t groups = (m + kUnpRows - 1) / kUnpRows;
-    for (int64_t gi = (int64_t)blockIdx.x * kUnpWarps + warp; gi < groups; gi += (int64_t)gridDim.x * kUnpWarps) {
-        const int64_t r0 = gi * kUnpRows;
-        uint4 y[kUnpRows][kMaxVec];          // the rows, then their modulated values, as bf16
+    if (warp == kUpWarps) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 64;" ::"r"(smem_u32(tmem_slot)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        tc_fence_before();
+    } else {
+        // ---------------- phase 1: LayerNorm statistics of rows 16 warp .. 16 warp + 15
+        const int rw = warp * 16;
+        const int64_t left = m - row0 - rw;
+        const int nr = left <= 0 ? 0 : (left >= 16 ? 16 : (int)left);   // live rows of this warp
+        uint8_t* ring = sm + (size_t)warp * nslot * row_bytes;
+        auto issue = [&](int i) {
+            const uint32_t bar = rbar0 + 8 * (i % nslot);
+            mbar_expect_tx(bar, row_bytes);
+            bulk_load(smem_u32(ring + (i % nslot) * row_bytes), x + (row0 + rw + i) * d, row_bytes, bar);
+        };
+        if (lane == 0)
+            for (int i = 0; i < nslot && i < nr; ++i) issue(i);
+        int i = 0;
+        bool ok = true;
+        for (; i < nr; ++i) {
+            ok = __all_sync(0xffffffffu, mbar_wait(rbar0 + 8 * (i % nslot), (i / nslot) & 1, abort_flag,
+                                                   &g_rowops_error, kErrUnpTimeout));
+            if (!ok) break;
+            const uint4* xs = reinterpret_cast<const uint4*>(ring + (i % nslot) * row_bytes);
+            uint4 y[VEC];
 #pragma unroll
-        for (int k = 0; k < kUnpRows; ++k) {     // both rows' loads in flight together
-            const uint4* xr = reinterpret_cast<const uint4*>(x + (r0 + k) * d);
-#pragma unroll
-            for (int i = 0; i < kMaxVec; ++i) {
-                const int vi = lane + 32 * i;
-                y[k][i] = (r0 + k < m && vi < nvec) ? __ldg(xr + vi) : make_uint4(0u, 0u, 0u, 0u);
+            for (int v = 0; v < VEC; ++v) {
+                const int vi = lane + 32 * v;
+                y[v] = vi < nvec ? xs[vi] : make_uint4(0u, 0u, 0u, 0u);
             }
-        }
-#pragma unroll
-        for (int k = 0; k < kUnpRows; ++k) {
-            if (r0 + k >= m) continue;       // warp-uniform: the pair's second row past m (zeros)
-            // LayerNorm statistics in the order of row_stats (same sums, same result)
+            __syncwarp();                                  // the slot may be refilled now
+            if (lane == 0 && i + nslot < nr) issue(i + nslot);
             float sum = 0.f;
 #pragma unroll
-            for (int i = 0; i < kMaxVec; ++i) {
-                if (lane + 32 * i >= nvec) continue;
-                float v[8];
-                unpack8(y[k][i], v);
+            for (int v = 0; v < VEC; ++v) {
+                if (lane + 32 * v >= nvec) continue;
+                float f[8];
+                unpack8(y[v], f);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) sum += v[j];
+                for (int j = 0; j < 8; ++j) sum += f[j];
             }
             const float mean = warp_sum(sum) / (float)d;
             float sq = 0.f;
 #pragma unroll
-            for (int i = 0; i < kMaxVec; ++i) {
-                if (lane + 32 * i >= nvec) continue;
-                float v[8];
-                unpack8(y[k][i], v);
+            for (int v = 0; v < VEC; ++v) {
+                if (lane + 32 * v >= nvec) continue;
+                float f[8];
+                unpack8(y[v], f);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) { const float t = v[j] - mean; sq += t * t; }
+                for (int j = 0; j < 8; ++j) { const float t = f[j] - mean; sq += t * t; }
             }
             const float rstd = rsqrtf(warp_sum(sq) / (float)d + 1e-6f);
+            if (lane == 0) stats[rw + i] = make_float2(mean, rstd);
+        }
+        if (lane == 0 && !ok) {
+            // a wait ran out: let the copies still in flight land before the slots are reused
+            volatile int no_abort = 0;
+            for (int k = i; k < nr && k < i + nslot; ++k)
+                mbar_wait(rbar0 + 8 * (k % nslot), (k / nslot) & 1, &no_abort, &g_rowops_error, kErrUnpTimeout);
+        }
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp < kUpWarps) {
+        // ---------------- phase 2 producers: thread tid owns 16-byte piece c = tid % 8 of rows
+        // tid / 8 + 32 h (h = 0..3) of every chunk, and splits 4 of the chunk's 16 x 64 weights
+        const int c = tid & 7, rr = tid >> 3;
+        const int wo = tid >> 4, wq = tid & 15;
+        float2 st[4];
+        const __nv_bfloat16* xr[4];
+        bool live[4];
 #pragma unroll
-            for (int i = 0; i < kMaxVec; ++i) {
-                const int vi = lane + 32 * i;
-                if (vi >= nvec) continue;
-                float v[8];
-                unpack8(y[k][i], v);
-                const float4 a0 = __ldg(reinterpret_cast<const float4*>(s1 + vi * 8));
-                const float4 a1 = __ldg(reinterpret_cast<const float4*>(s1 + vi * 8 + 4));
-                const float4 b0 = __ldg(reinterpret_cast<const float4*>(sh + vi * 8));
-                const float4 b1 = __ldg(reinterpret_cast<const float4*>(sh + vi * 8 + 4));
-                const float sa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                const float sb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        for (int h = 0; h < 4; ++h) {
+            live[h] = row0 + rr + 32 * h < m;
+            st[h] = stats[rr + 32 * h];
+            xr[h] = x + (live[h] ? row0 + rr + 32 * h : 0) * d;
+        }
+        bool ok = !*abort_flag;
+#pragma unroll 1
+        for (int k0 = 0; ok && k0 < nk; k0 += kUpRound) {
+            uint4 raw[kUpRound][4];
+            float4 wv[kUpRound];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = (v[j] - mean) * rstd * sa[j] + sb[j];
-                y[k][i] = pack8(v);
+            for (int g = 0; g < kUpRound; ++g) {
+                const int col = (k0 + g) * kUpK + 8 * c;
+                const bool cok = k0 + g < nk && col < d;
+#pragma unroll
+                for (int h = 0; h < 4; ++h)
+                    raw[g][h] = (cok && live[h]) ? __ldg(reinterpret_cast<const uint4*>(xr[h] + col))
+                                                 : make_uint4(0u, 0u, 0u, 0u);
+                const int wc = (k0 + g) * kUpK + 4 * wq;
+                wv[g] = (k0 + g < nk && wc < d) ? __ldg(reinterpret_cast<const float4*>(w + (int64_t)wo * d + wc))
+                                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int g = 0; g < kUpRound; ++g) {
+                const int k = k0 + g;
+                if (k >= nk) break;
+                const int s = k % kUpStages;
+                if (k >= kUpStages &&
+                    !__all_sync(0xffffffffu, mbar_wait(empty(s), ((k / kUpStages) - 1) & 1, abort_flag,
+                                                       &g_rowops_error, kErrUnpTimeout))) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* stg = sm + s * kUpStageBytes;
+                const int col = k * kUpK + 8 * c;
+                if (col < d) {
+                    const float4 a0 = *reinterpret_cast<const float4*>(s1_s + col);
+                    const float4 a1 = *reinterpret_cast<const float4*>(s1_s + col + 4);
+                    const float4 b0 = *reinterpret_cast<const float4*>(sh_s + col);
+                    const float4 b1 = *reinterpret_cast<const float4*>(sh_s + col + 4);
+                    const float sa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                    const float sb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                        if (live[h]) {
+                            float f[8];
+                            unpack8(raw[g][h], f);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) f[j] = (f[j] - st[h].x) * st[h].y * sa[j] + sb[j];
+                            v = pack8(f);
+                        }
+                        *reinterpret_cast<uint4*>(stg + up_swz(rr + 32 * h, c)) = v;
+                    }
+                } else {
+#pragma unroll
+                    for (int h = 0; h < 4; ++h)
+                        *reinterpret_cast<uint4*>(stg + up_swz(rr + 32 * h, c)) = make_uint4(0u, 0u, 0u, 0u);
+                }
+                {
+                    // weights w[wo, 4 wq .. 4 wq + 3] of the chunk -> B rows wo, 16 + wo, 32 + wo
+                    float r[4] = {wv[g].x, wv[g].y, wv[g].z, wv[g].w};
+#pragma unroll
+                    for (int part = 0; part < 3; ++part) {
+                        __nv_bfloat162 lo2 = __floats2bfloat162_rn(r[0], r[1]), hi2 = __floats2bfloat162_rn(r[2], r[3]);
+                        r[0] -= __low2float(lo2);
+                        r[1] -= __high2float(lo2);
+                        r[2] -= __low2float(hi2);
+                        r[3] -= __high2float(hi2);
+                        const int n = 16 * part + wo;
+                        uint2 pk;
+                        pk.x = *reinterpret_cast<uint32_t*>(&lo2);
+                        pk.y = *reinterpret_cast<uint32_t*>(&hi2);
+                        *reinterpret_cast<uint2*>(stg + kUpABytes + up_swz(n, wq >> 1) + (wq & 1) * 8) = pk;
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor core
+                __syncwarp();
+                if (lane == 0) mbar_arrive(full(s));
             }
         }
-        float acc[kUnpRows * 16];
+    } else {
+        // ---------------- MMA issuer (converged warp, elected lane)
+        const uint64_t a0 = make_desc(smem_u32(sm), 16, 1024, kSw128);
+        const uint64_t b0 = make_desc(smem_u32(sm + kUpABytes), 16, 1024, kSw128);
+        constexpr uint32_t kIdesc = make_idesc(kUpRows, kUpN, false);
+        bool ok = true;
+        for (int k = 0; k < nk; ++k) {
+            const int s = k % kUpStages;
+            if (!__all_sync(0xffffffffu, mbar_wait(full(s), (k / kUpStages) & 1, abort_flag, &g_rowops_error,
+                                                   kErrUnpTimeout))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint64_t so = (uint64_t)(s * (kUpStageBytes >> 4));
 #pragma unroll
-        for (int t = 0; t < kUnpRows * 16; ++t) acc[t] = 0.f;
+            for (int kk = 0; kk < kUpK / 16; ++kk)
+                tc_mma_elect(tmem, a0 + so + kk * 2, b0 + so + kk * 2, kIdesc, (k > 0 || kk > 0) ? 1u : 0u);
+            tc_commit_elect(empty(s));
+        }
+        if (ok) tc_commit_elect(done);
+    }
+
+    // ---------------- epilogue: warp q reads TMEM lanes 32q .. 32q + 31 (the tile's rows)
+    if (warp < 4) {
+        if (__all_sync(0xffffffffu, mbar_wait(done, 0, abort_flag, &g_rowops_error, kErrUnpTimeout))) {
+            tc_fence_after();
+            float v[64];
+            const uint32_t ta = tmem + ((uint32_t)(32 * warp) << 16);
+            tmem_ld32(ta, v);
+            tmem_ld32(ta + 32, v + 32);
+            tmem_wait_ld();
+            const int64_t row = row0 + 32 * warp + lane;
+            if (row < m) {
+                float4* dst = reinterpret_cast<float4*>(out + row * 16);
 #pragma unroll
-        for (int i = 0; i < kMaxVec; ++i) {
-            const int vi = lane + 32 * i;
-            if (vi >= nvec) continue;
-            float yv[kUnpRows][8];
+                for (int q = 0; q < 4; ++q) {
+                    float o[4];
 #pragma unroll
-            for (int k = 0; k < kUnpRows; ++k) unpack8(y[k][i], yv[k]);
-#pragma unroll
-            for (int o = 0; o < 16; ++o) {
-                const float4 w0 = w_s[(2 * o) * nvec + vi], w1 = w_s[(2 * o + 1) * nvec + vi];
-                const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-                for (int k = 0; k < kUnpRows; ++k)
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) acc[k * 16 + o] = fmaf(yv[k][j], wv[j], acc[k * 16 + o]);
+                    for (int e = 0; e < 4; ++e) o[e] = (v[32 + 4 * q + e] + v[16 + 4 * q + e]) + v[4 * q + e];
+                    dst[q] = make_float4(o[0], o[1], o[2], o[3]);
+                }
             }
         }
-        // reduce-scatter: after the step with offset `off`, a lane keeps the half of its
-        // values whose index has the lane's `off` bit
-#pragma unroll
-        for (int off = 16, nkeep = 16; off >= 1; off >>= 1, nkeep >>= 1) {
-            const bool upper = (lane & off) != 0;
-#pragma unroll
-            for (int j = 0; j < nkeep; ++j) {
-                const float send = upper ? acc[j] : acc[j + nkeep];
-                const float keep = upper ? acc[j + nkeep] : acc[j];
-                acc[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-            }
-        }
-        const int64_t row = r0 + (lane >> 4);
-        if (row < m) out[row * 16 + (lane & 15)] = acc[0];
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kUpWarps) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 64;" ::"r"(tmem));
     }
 }
 
@@ -589,16 +761,15 @@ __global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ h, int64_t m, in
     store8(out + row * f + c, o);
 }
 
-// x[n, d] = xt[n,16] @ w[d,16]^T.  A block owns 64 output channels for many rows:
-// their 64x16 weights sit in registers (lane = one output channel pair), each
-// warp streams rows, reading a row's 16 inputs once (broadcast) and writing
-// 64 outputs per row.
-// x[r, c] = sum_i xt[r, i] * w[c, i] (16 inputs, fp32 FMAs in order i = 0..15), bf16 out.
-// A CTA takes 64 output channels (lane l: channels c0 = 64 bx + 2l and c0 + 1, their 32
-// weights in registers) of kPatchRows rows: the rows' xt (64 bytes each) is staged in
-// shared memory by one round of 16-byte loads issued by all threads, then each warp
-// computes every eighth row with packed FMAs (both channels in one fp32x2 FMA).
+// x[r, c] = sum_i xt[r, i] * w[c, i] (16 fp32 inputs per row), bf16 out.  A CTA takes 128
+// output channels (lane l: channels c0 = 128 bx + 4l .. c0 + 3, their 64 weights in registers as
+// (even input, odd input) pairs) of kPatchRows rows: the rows' xt (64 bytes each) is staged in
+// shared memory by one round of 16-byte loads issued by all threads, then each warp computes
+// every eighth row.  A channel's sum runs as one packed fp32x2 FMA chain over the input pairs
+// (2i, 2i + 1), the even and odd halves added at the end: 32 packed FMAs per row and lane for 4
+// outputs, the row's inputs read from shared memory as pairs without repacking.
 constexpr int kPatchRows = 512;
+constexpr int kPatchCols = 128;
 
 __global__ void __launch_bounds__(256) patchify_kernel(const float* __restrict__ xt, int64_t n,
                                                        const float* __restrict__ w, int d,
@@ -619,33 +790,44 @@ __global__ void __launch_bounds__(256) patchify_kernel(const float* __restrict__
         const int q = tid + b * 256;
         if (q < rows * 4) xs[q] = t[b];
     }
-    const int c0 = blockIdx.x * 64 + lane * 2;
-    float2 wv[16];
+    const int c0 = blockIdx.x * kPatchCols + lane * 4;
+    float2 wv[4][8];                          // wv[ch][i] = (w[c0 + ch, 2i], w[c0 + ch, 2i + 1])
     if (c0 < d) {
-        const float4* wa = reinterpret_cast<const float4*>(w + (int64_t)c0 * 16);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float4 a = __ldg(wa + q), b = __ldg(wa + 4 + q);   // rows c0 and c0 + 1
-            wv[4 * q + 0] = make_float2(a.x, b.x);
-            wv[4 * q + 1] = make_float2(a.y, b.y);
-            wv[4 * q + 2] = make_float2(a.z, b.z);
-            wv[4 * q + 3] = make_float2(a.w, b.w);
+        for (int ch = 0; ch < 4; ++ch) {
+            const float4* wa = reinterpret_cast<const float4*>(w + (int64_t)(c0 + ch) * 16);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 a = __ldg(wa + q);
+                wv[ch][2 * q] = make_float2(a.x, a.y);
+                wv[ch][2 * q + 1] = make_float2(a.z, a.w);
+            }
         }
     }
     __syncthreads();
     if (c0 >= d) return;
 #pragma unroll 2
     for (int r = warp; r < rows; r += 8) {
-        float xv[16];
+        float2 xv[8];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            const float4 t = xs[r * 4 + q];
-            xv[4 * q] = t.x; xv[4 * q + 1] = t.y; xv[4 * q + 2] = t.z; xv[4 * q + 3] = t.w;
+            const float4 v = xs[r * 4 + q];
+            xv[2 * q] = make_float2(v.x, v.y);
+            xv[2 * q + 1] = make_float2(v.z, v.w);
         }
-        float2 acc = make_float2(0.f, 0.f);
+        float o[4];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc = tc::ffma2v(make_float2(xv[i], xv[i]), wv[i], acc);
-        *reinterpret_cast<__nv_bfloat162*>(out + (r0 + r) * d + c0) = __floats2bfloat162_rn(acc.x, acc.y);
+        for (int ch = 0; ch < 4; ++ch) {
+            float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc = tc::ffma2v(xv[i], wv[ch][i], acc);
+            o[ch] = acc.x + acc.y;
+        }
+        __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]), hi = __floats2bfloat162_rn(o[2], o[3]);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&lo);
+        pk.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(out + (r0 + r) * d + c0) = pk;
     }
 }
 
@@ -706,7 +888,7 @@ int launch_gate_add_staged(__nv_bfloat16* x, const __nv_bfloat16* h, int64_t h_s
         return VDIT_ERR_LAUNCH;
     }
     constexpr size_t kMaxSmem = 227 * 1024 - 256;
-    const size_t per_warp = (size_t)8 * d + 16;
+    const size_t per_warp = (size_t)8 * d + 32;         // four row slots and four barriers
     const int nwarps = (int)std::min<size_t>(kGaMaxWarps, (kMaxSmem - (size_t)kGaVecBytes * d) / per_warp);
     if (sms[dev] == 0) {
         int n = 0;
@@ -732,7 +914,7 @@ extern "C" int vdit_patchify(const float* xt, int64_t n, const float* w, int32_t
     if (!aligned16(xt) || !aligned16(w) || !aligned16(x_out)) return VDIT_ERR_ALIGN;
     if (n == 0) return VDIT_OK;
     if (d % 2) return VDIT_ERR_UNSUPPORTED;
-    patchify_kernel<<<dim3((d + 63) / 64, (unsigned)((n + kPatchRows - 1) / kPatchRows)), 256, 0,
+    patchify_kernel<<<dim3((d + kPatchCols - 1) / kPatchCols, (unsigned)((n + kPatchRows - 1) / kPatchRows)), 256, 0,
                       static_cast<cudaStream_t>(stream)>>>(xt, n, w, d, static_cast<__nv_bfloat16*>(x_out));
     count_launches(1);
     return check_launch();
@@ -790,34 +972,28 @@ extern "C" int vdit_gate_add2_modulate(void* x, const void* h, int64_t h_stride,
 extern "C" int vdit_out_modulate_unpatchify(const void* x, int64_t m, int32_t d, const float* s1, const float* sh,
                                             const float* w, float* out, vdit_stream_t stream) {
     if (m < 0 || !row_width_ok(d) || !x || !s1 || !sh || !w || !out) return VDIT_ERR_ARG;
-    if (!aligned16(x) || !aligned16(w) || !aligned16(s1) || !aligned16(sh)) return VDIT_ERR_ALIGN;
+    if (!aligned16(x) || !aligned16(w) || !aligned16(s1) || !aligned16(sh) || !aligned16(out)) return VDIT_ERR_ALIGN;
     if (m == 0) return VDIT_OK;
-    static int sms[64] = {0};
+    static bool attr_set[64] = {false};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess || dev < 0 || dev >= 64) {
         if (e != cudaSuccess) record_cuda_error(e);
         return VDIT_ERR_LAUNCH;
     }
-    const size_t smem = (size_t)16 * d * sizeof(float);      // the staged weight (<= 128 KB)
-    constexpr int kMaxUnpSmem = 16 * 256 * kMaxVec * (int)sizeof(float);
-    if (sms[dev] == 0) {
-        int n = 0, per_sm = 0;
-        e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (!attr_set[dev]) {
+        e = cudaFuncSetAttribute(out_unpatchify_kernel<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, kUpSmem);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(out_unpatchify_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxUnpSmem);
-        if (e == cudaSuccess)   // resident CTAs per SM at the largest weight (registers limit it to one)
-            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, out_unpatchify_kernel, kUnpWarps * 32,
-                                                              kMaxUnpSmem);
-        if (e != cudaSuccess || per_sm < 1) {
-            record_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidConfiguration);
+            e = cudaFuncSetAttribute(out_unpatchify_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kUpSmem);
+        if (e != cudaSuccess) {
+            record_cuda_error(e);
             return VDIT_ERR_LAUNCH;
         }
-        sms[dev] = n * per_sm;
+        attr_set[dev] = true;
     }
-    const int64_t groups = (m + kUnpRows - 1) / kUnpRows;
-    const unsigned grid = (unsigned)std::min<int64_t>((groups + kUnpWarps - 1) / kUnpWarps, (int64_t)sms[dev]);
-    out_unpatchify_kernel<<<grid, kUnpWarps * 32, smem, static_cast<cudaStream_t>(stream)>>>(
+    const int64_t tiles = (m + kUpRows - 1) / kUpRows;
+    const auto kernel = d <= 256 * 6 ? out_unpatchify_kernel<6> : out_unpatchify_kernel<8>;
+    kernel<<<(unsigned)tiles, (kUpWarps + 1) * 32, kUpSmem, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16*>(x), m, d, s1, sh, w, out);
     count_launches(1);
     return check_launch();

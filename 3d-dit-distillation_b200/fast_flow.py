@@ -42,6 +42,7 @@ KERNEL_CLASSES = {
     "attention_context_to_voxel": "tensor", "attention_context_self": "tensor",
     "gemm_qkv_fused": "tensor", "gemm_voxel": "tensor", "gemm_context": "tensor",
     "dwconv27_swiglu": "hbm", "gate_add_modulate": "hbm", "single_query_context_to_voxel": "hbm",
+    "unpatchify_project": "hbm",
 }
 
 
@@ -138,6 +139,7 @@ class OptimizedLatDitRunner:
 
         self.W_patch = f32("flow.patchify.weight")                 # [D, 16]
         self.W_unpatch = f32("flow.unpatchify.weight")             # [16, D]
+        self.W_unpatch3 = fk.split_weight3(self.W_unpatch)         # [48, D] bf16 hi / mid / lo parts
         self.W_image = bf("image_map.weight")
         self.b_image = bf("image_map.bias")
         self.W_t0, self.b_t0 = f32("flow.time_embed.0.weight"), f32("flow.time_embed.0.bias")
@@ -245,6 +247,12 @@ class OptimizedLatDitRunner:
         nb = x.shape[0] * x.shape[1] * 2.0 * (3 if broadcast_h else 4)
         return self._run("gate_add_modulate", nb, fk.fast_gate_add_and_modulate, x, h, g, s1, sh,
                          broadcast_h=broadcast_h)
+
+    def _unpatchify(self, y: torch.Tensor) -> torch.Tensor:
+        """[N,16] fp32 velocity from the output-modulated rows y = bf16(LN(x) * s1 + sh): the
+        projection of ``lib/fast_kernels.py:613-648`` with its fp32 weight (bytes: y read, out written)."""
+        return self._run("unpatchify_project", y.shape[0] * (y.shape[1] * 2.0 + 64.0), fk.unpatchify_project, y,
+                         self.W_unpatch3)
 
     def _get_rope_2d_table(self, cond_size: int):
         if cond_size not in self._rope_2d_cache:
@@ -426,13 +434,12 @@ class OptimizedLatDitRunner:
                 hx = self._lin(ox, w["to_out_cross"], w["to_out_cross_b"])
                 h_mod = self._gate_add_mod(x, hx, G[b, 5], G[b, 6], G[b, 7])
             hf = self._ffn(b, h_mod, geom)
-            if b + 1 < self.depth:
-                h_mod = self._gate_add_mod(x, hf, G[b, 8], G[b + 1, 0], G[b + 1, 1])
-            else:
-                fk.fast_gate_add(x, hf, G[b, 8])
+            # after the last block the gate-add modulates with the output norm's scale and shift
+            nxt = (G[b + 1, 0], G[b + 1, 1]) if b + 1 < self.depth else (OG[0], OG[1])
+            h_mod = self._gate_add_mod(x, hf, G[b, 8], *nxt)
         if side is not main:
             main.wait_stream(side)
-        return fk.fast_out_modulate_unpatchify(x, None, OG[0], OG[1], self.W_unpatch)
+        return self._unpatchify(h_mod)
 
     def _frozen_context_kv(self, c: torch.Tensor, CG2) -> list:
         """K/V of the frozen context for every block after the context blocks, queued on the
@@ -558,13 +565,11 @@ class OptimizedLatDitRunner:
                 else:
                     h_mod = self._gate_add_mod(x, x_const, G[b, 5], G[b, 6], G[b, 7], broadcast_h=True)
             hf = self._ffn(b, h_mod, geom)
-            if b + 1 < self.depth:
-                h_mod = self._gate_add_mod(x, hf, G[b, 8], G[b + 1, 0], G[b + 1, 1])
-            else:
-                fk.fast_gate_add(x, hf, G[b, 8])
+            nxt = (G[b + 1, 0], G[b + 1, 1]) if b + 1 < self.depth else (OG[0], OG[1])
+            h_mod = self._gate_add_mod(x, hf, G[b, 8], *nxt)
         if two:
             main.wait_stream(side)
-        return fk.fast_out_modulate_unpatchify(x, None, OG[0], OG[1], self.W_unpatch)
+        return self._unpatchify(h_mod)
 
     # ------------------------------------------------------------------ sampler
     @torch.no_grad()

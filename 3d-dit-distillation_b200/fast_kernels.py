@@ -205,6 +205,23 @@ def fast_out_modulate_unpatchify(x: torch.Tensor, sizes, scale1: torch.Tensor, s
     return out
 
 
+def split_weight3(w_fp32: torch.Tensor) -> torch.Tensor:
+    """[3R, D] bf16 three-part split of an fp32 [R, D] weight (hi, mid, lo row blocks)."""
+    r, d = w_fp32.shape
+    w3 = torch.empty(3 * r, d, dtype=torch.bfloat16, device=w_fp32.device)
+    check(lib().vdit_split_weight3(ptr(w_fp32), r, d, ptr(w3), _s(w_fp32)), "split_weight3")
+    return w3
+
+
+def unpatchify_project(y: torch.Tensor, w3: torch.Tensor) -> torch.Tensor:
+    """[N,16] fp32 = y (bf16, already modulated) @ w^T at fp32 accuracy, w as its split ``w3``
+    (the projection of ``lib/fast_kernels.py:613-648``)."""
+    m, d = y.shape
+    out = torch.empty(m, 16, dtype=torch.float32, device=y.device)
+    check(lib().vdit_unpatchify_project(ptr(y), m, d, ptr(w3), ptr(out), _s(y)), "unpatchify_project")
+    return out
+
+
 def fused_qknorm_rope3d_gather(qkv: torch.Tensor, q_scale: torch.Tensor, k_scale: torch.Tensor,
                                cos_t: torch.Tensor, sin_t: torch.Tensor, h_coords: torch.Tensor,
                                fwd_idx: Optional[torch.Tensor], heads: int, head_dim: int,

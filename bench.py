@@ -330,7 +330,7 @@ def hbm_bench(w, reps: int = 10):
     alone with CUDA events after a 256 MiB L2 flush; median of ``reps`` launches after two
     warm-up launches.  Algorithmic bytes (each tensor counted once):
     gate-add + LN + AdaLN 4*N*D*2; LN + AdaLN 2*N*D*2; QK-norm/RoPE/gather 2*3*N*D*2 + 8N;
-    out-modulate-unpatchify N*D*2 + N*16*4; patchify N*16*4 + N*D*2; single query over
+    out-modulate-unpatchify and the unpatchify projection N*D*2 + N*16*4; patchify N*16*4 + N*D*2; single query over
     formed K/V 2*N*D*2; single query over the voxel rows N*D*2 + 2*D*D*2 (W_k, W_v)."""
     from vdit import fast_kernels as fk
     from vdit.workloads import shell_voxels, uniform_voxels
@@ -386,8 +386,11 @@ def hbm_bench(w, reps: int = 10):
                    lambda: fk.fused_qknorm_rope3d_gather(qkv, qs, qs, cos, sin, hc, fwd[0], H, HD, out=qkv_o),
                    2 * 3 * n * D * 2 + 8 * n))
     wu = torch.randn(16, D, device="cuda", generator=g) * 0.02
-    out.append(row("out LN + AdaLN + unpatchify", "out_unpatchify_kernel",
+    out.append(row("out LN + AdaLN + unpatchify (one call)", "out_unpatchify_kernel<6>",
                    lambda: fk.fast_out_modulate_unpatchify(x, None, s1, sh, wu), n * D * 2 + n * 16 * 4))
+    wu3 = fk.split_weight3(wu)
+    out.append(row("unpatchify projection of the modulated rows (the runner's path)", "unpatchify_project_kernel",
+                   lambda: fk.unpatchify_project(mod, wu3), n * D * 2 + n * 16 * 4))
     xt = torch.randn(n, 16, device="cuda", generator=g)
     wp = torch.randn(D, 16, device="cuda", generator=g) * 0.02
     out.append(row("patchify", "patchify_kernel", lambda: fk.patchify(xt, wp), n * 16 * 4 + n * D * 2))

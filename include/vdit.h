@@ -116,6 +116,19 @@ int vdit_out_modulate_unpatchify(const void* x, int64_t m, int32_t d, const floa
                                  const float* shift, const float* w, float* out,
                                  vdit_stream_t stream);
 
+/* The unpatchify projection alone, for rows already modulated (the last block's fused gate-add +
+ * LayerNorm + AdaLN with the output modulation): out[m,16] fp32 = y[m,d] (bf16) @ w[16,d]^T at
+ * fp32 accuracy on the tensor cores, w given as its three-part bf16 split w3 [48,d] from
+ * vdit_split_weight3.  y, w3, out 16-byte aligned; d % 8 == 0; m < 2^31.  The projection of
+ * lib/fast_kernels.py:613-648 (its fp32 weight, lib/fast_flow.py:144-148). */
+int vdit_unpatchify_project(const void* y, int64_t m, int32_t d, const void* w3, float* out,
+                            vdit_stream_t stream);
+
+/* w3[3*rows, d] bf16 = the three-part split of w[rows, d] fp32: row p*rows + o holds part p of
+ * row o, hi = bf16(w), mid = bf16(w - hi), lo = bf16(w - hi - mid) (hi + mid + lo = w to fp32
+ * precision).  Made once per weight for vdit_unpatchify_project (rows = 16). */
+int vdit_split_weight3(const float* w, int32_t rows, int32_t d, void* w3, vdit_stream_t stream);
+
 /* out[j] = (RoPE3D(RMS(q[src])*q_scale), RoPE3D(RMS(k[src])*k_scale), v[src]),
  * src = fwd[j] (NULL: identity).  qkv/out bf16 [n,3,heads,head_dim];
  * q_scale/k_scale fp32 [heads,head_dim]; cos/sin fp32 [res, head_dim/6];

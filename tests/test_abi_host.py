@@ -60,6 +60,11 @@ def test_shape_errors_are_reported_before_any_launch():
     assert lib.vdit_dwconv27_swiglu_planned(16, 5, 960, 16, 16, 16, 16, None) == -4   # c % 128 != 0
     assert lib.vdit_dwconv27_swiglu_planned_bf16w(None, 5, 7680, None, None, None, None, None) == -1
     assert lib.vdit_dwconv27_swiglu_planned_bf16w(16, 5, 960, 16, 16, 16, 16, None) == -4
+    assert lib.vdit_unpatchify_project(None, 10, 1536, None, None, None) == -1
+    assert lib.vdit_unpatchify_project(16, 10, 1540, 16, 16, None) == -1           # d % 8 != 0
+    assert lib.vdit_unpatchify_project(8, 10, 1536, 16, 16, None) == -2            # y not 16-byte aligned
+    assert lib.vdit_unpatchify_project(16, 0, 1536, 16, 16, None) == 0             # nothing to do
+    assert lib.vdit_split_weight3(None, 16, 1536, None, None) == -1
     with pytest.raises(RuntimeError, match="invalid argument"):
         _lib.check(-1, "probe")
 

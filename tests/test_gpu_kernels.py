@@ -154,7 +154,7 @@ def test_gate_add_staged_matches_rowwise(m, d, stride_h):
 
 @pytest.mark.parametrize("m,d", [(777, 1536), (1, 1536), (16384, 1536), (301, 1000), (64, 2048)])
 def test_out_modulate_unpatchify(m, d):
-    """Rows in pairs (odd m leaves a half pair), d not a multiple of 256 leaves lanes idle."""
+    """Ragged 128-row tiles (m % 128), a ragged last 64-column chunk (d = 1000), one row."""
     g = torch.Generator(device=DEV).manual_seed(3 + m + d)
     x = torch.randn(m, d, device=DEV, generator=g).to(torch.bfloat16)
     s1 = 1 + 0.1 * torch.randn(d, device=DEV, generator=g)
@@ -163,9 +163,38 @@ def test_out_modulate_unpatchify(m, d):
     out = fk.fast_out_modulate_unpatchify(x, None, s1, sh, w)
     mod = (om.layer_norm(x.float()) * s1 + sh).to(torch.bfloat16).float()   # rounded as the reference does
     ref = mod @ w.t()
-    assert out.dtype == torch.float32 and out.shape == (m, 16) and rel(out, ref) < 1e-4
+    # fp32 accuracy from the three-part bf16 split of the weight (bf16 weights alone: ~2e-3)
+    assert out.dtype == torch.float32 and out.shape == (m, 16) and rel(out, ref) < 5e-5
     for r in (0, m - 1):                                                    # each row on its own
         assert rel(out[r], ref[r]) < 1e-4
+
+
+def test_split_weight3_is_exact():
+    """hi + mid + lo reproduces every fp32 weight (three bf16 parts carry the 24-bit significand)."""
+    g = torch.Generator(device=DEV).manual_seed(11)
+    w = torch.randn(16, 1536, device=DEV, generator=g) * torch.logspace(-4, 2, 1536, device=DEV)
+    w3 = fk.split_weight3(w)
+    assert w3.dtype == torch.bfloat16 and w3.shape == (48, 1536)
+    parts = w3.double().reshape(3, 16, 1536)
+    assert torch.equal(parts.sum(0), w.double())
+    assert torch.equal(w3[:16], w.to(torch.bfloat16))                    # hi = bf16(w)
+
+
+@pytest.mark.parametrize("m,d", [(777, 1536), (1, 1536), (16384, 1536), (301, 1000), (64, 2048), (130, 8)])
+def test_unpatchify_project(m, d):
+    """The projection alone on modulated rows: ragged row tiles (m % 128), a ragged last column
+    chunk (d % 64), fp32-accurate against a float64 product (bf16 weights would miss by ~2e-3)."""
+    g = torch.Generator(device=DEV).manual_seed(5 + m + d)
+    x = torch.randn(m, d, device=DEV, generator=g).to(torch.bfloat16)
+    s1 = 1 + 0.1 * torch.randn(d, device=DEV, generator=g)
+    sh = 0.1 * torch.randn(d, device=DEV, generator=g)
+    w = 0.05 * torch.randn(16, d, device=DEV, generator=g)
+    y = fk.fast_modulate(x, None, s1, sh)
+    out = fk.unpatchify_project(y, fk.split_weight3(w))
+    ref = y.double() @ w.double().t()
+    assert out.dtype == torch.float32 and out.shape == (m, 16) and rel(out, ref) < 5e-5
+    fused = fk.fast_out_modulate_unpatchify(x, None, s1, sh, w)           # the one-call fused form
+    assert rel(out, fused) < 5e-5
 
 
 @pytest.mark.parametrize("n,d", [(500, 1536), (16384, 1536), (1, 64), (1025, 200)])
