@@ -481,6 +481,7 @@ int dwconv_plan_error_word(int clear);  // error word of the staged depthwise co
 int rowops_error_word(int clear);       // error word of the staged row kernels (rowops.cu)
 int gemm_error_word(int clear);         // error word of the tcgen05 GEMM (gemm.cu)
 int unpatch_error_word(int clear);      // error word of the unpatchify projection (unpatchify.cu)
+int patchify_error_word(int clear);     // error word of the tensor-core patchify (patchify.cu)
 }
 
 extern "C" int vdit_device_error(int clear) {
@@ -501,5 +502,9 @@ extern "C" int vdit_device_error(int clear) {
     if (g < 0) return g;
     const int u = vdit::unpatch_error_word(clear);
     if (u < 0) return u;
-    return v != 0 ? v : (d != 0 ? d : (p != 0 ? p : (r != 0 ? r : (g != 0 ? g : u))));
+    const int t = vdit::patchify_error_word(clear);
+    if (t < 0) return t;
+    for (int w : {v, d, p, r, g, u, t})
+        if (w != 0) return w;
+    return 0;
 }

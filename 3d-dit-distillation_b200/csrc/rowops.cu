@@ -31,21 +31,26 @@ __device__ __forceinline__ void row_load(const __nv_bfloat16* __restrict__ row, 
     }
 }
 
+// Mean and 1/sqrt(var + 1e-6) of a row, two-pass.  A lane's values are summed in four
+// interleaved partial sums (element j of each vector into sum j % 4, combined as (s0 + s1) +
+// (s2 + s3)), which keeps four independent add chains in flight instead of one.
+__device__ __forceinline__ float sum4(const float (&s)[4]) { return (s[0] + s[1]) + (s[2] + s[3]); }
+
 __device__ __forceinline__ void row_stats(const RowRegs& r, int nvec, int lane, int d, float& mean, float& rstd) {
-    float s = 0.f;
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int i = 0; i < kMaxVec; ++i)
         if (lane + 32 * i < nvec)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) s += r.v[i][j];
-    mean = warp_sum(s) / (float)d;
-    float q = 0.f;
+            for (int j = 0; j < 8; ++j) s[j & 3] += r.v[i][j];
+    mean = warp_sum(sum4(s)) / (float)d;
+    float q[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int i = 0; i < kMaxVec; ++i)
         if (lane + 32 * i < nvec)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) { float t = r.v[i][j] - mean; q += t * t; }
-    rstd = rsqrtf(warp_sum(q) / (float)d + 1e-6f);
+            for (int j = 0; j < 8; ++j) { float t = r.v[i][j] - mean; q[j & 3] += t * t; }
+    rstd = rsqrtf(warp_sum(sum4(q)) / (float)d + 1e-6f);
 }
 
 __device__ __forceinline__ void row_modulate_store(const RowRegs& r, int nvec, int lane, float mean, float rstd,
@@ -403,26 +408,26 @@ __global__ void __launch_bounds__((kUpWarps + 1) * 32, 1) out_unpatchify_kernel(
             }
             __syncwarp();                                  // the slot may be refilled now
             if (lane == 0 && i + nslot < nr) issue(i + nslot);
-            float sum = 0.f;
+            float sum[4] = {0.f, 0.f, 0.f, 0.f};       // the partial sums of row_stats
 #pragma unroll
             for (int v = 0; v < VEC; ++v) {
                 if (lane + 32 * v >= nvec) continue;
                 float f[8];
                 unpack8(y[v], f);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) sum += f[j];
+                for (int j = 0; j < 8; ++j) sum[j & 3] += f[j];
             }
-            const float mean = warp_sum(sum) / (float)d;
-            float sq = 0.f;
+            const float mean = warp_sum(sum4(sum)) / (float)d;
+            float sq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int v = 0; v < VEC; ++v) {
                 if (lane + 32 * v >= nvec) continue;
                 float f[8];
                 unpack8(y[v], f);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) { const float t = f[j] - mean; sq += t * t; }
+                for (int j = 0; j < 8; ++j) { const float t = f[j] - mean; sq[j & 3] += t * t; }
             }
-            const float rstd = rsqrtf(warp_sum(sq) / (float)d + 1e-6f);
+            const float rstd = rsqrtf(warp_sum(sum4(sq)) / (float)d + 1e-6f);
             if (lane == 0) stats[rw + i] = make_float2(mean, rstd);
         }
         if (lane == 0 && !ok) {
@@ -761,76 +766,6 @@ __global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ h, int64_t m, in
     store8(out + row * f + c, o);
 }
 
-// x[r, c] = sum_i xt[r, i] * w[c, i] (16 fp32 inputs per row), bf16 out.  A CTA takes 128
-// output channels (lane l: channels c0 = 128 bx + 4l .. c0 + 3, their 64 weights in registers as
-// (even input, odd input) pairs) of kPatchRows rows: the rows' xt (64 bytes each) is staged in
-// shared memory by one round of 16-byte loads issued by all threads, then each warp computes
-// every eighth row.  A channel's sum runs as one packed fp32x2 FMA chain over the input pairs
-// (2i, 2i + 1), the even and odd halves added at the end: 32 packed FMAs per row and lane for 4
-// outputs, the row's inputs read from shared memory as pairs without repacking.
-constexpr int kPatchRows = 512;
-constexpr int kPatchCols = 128;
-
-__global__ void __launch_bounds__(256) patchify_kernel(const float* __restrict__ xt, int64_t n,
-                                                       const float* __restrict__ w, int d,
-                                                       __nv_bfloat16* __restrict__ out) {
-    __shared__ float4 xs[kPatchRows * 4];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t r0 = (int64_t)blockIdx.y * kPatchRows;
-    const int rows = (int)(n - r0 < kPatchRows ? n - r0 : (int64_t)kPatchRows);
-    const float4* src = reinterpret_cast<const float4*>(xt + r0 * 16);
-    float4 t[kPatchRows * 4 / 256];          // every load in flight before the first store
-#pragma unroll
-    for (int b = 0; b < kPatchRows * 4 / 256; ++b) {
-        const int q = tid + b * 256;
-        if (q < rows * 4) t[b] = __ldg(src + q);
-    }
-#pragma unroll
-    for (int b = 0; b < kPatchRows * 4 / 256; ++b) {
-        const int q = tid + b * 256;
-        if (q < rows * 4) xs[q] = t[b];
-    }
-    const int c0 = blockIdx.x * kPatchCols + lane * 4;
-    float2 wv[4][8];                          // wv[ch][i] = (w[c0 + ch, 2i], w[c0 + ch, 2i + 1])
-    if (c0 < d) {
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-            const float4* wa = reinterpret_cast<const float4*>(w + (int64_t)(c0 + ch) * 16);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float4 a = __ldg(wa + q);
-                wv[ch][2 * q] = make_float2(a.x, a.y);
-                wv[ch][2 * q + 1] = make_float2(a.z, a.w);
-            }
-        }
-    }
-    __syncthreads();
-    if (c0 >= d) return;
-#pragma unroll 2
-    for (int r = warp; r < rows; r += 8) {
-        float2 xv[8];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float4 v = xs[r * 4 + q];
-            xv[2 * q] = make_float2(v.x, v.y);
-            xv[2 * q + 1] = make_float2(v.z, v.w);
-        }
-        float o[4];
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-            float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) acc = tc::ffma2v(xv[i], wv[ch][i], acc);
-            o[ch] = acc.x + acc.y;
-        }
-        __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]), hi = __floats2bfloat162_rn(o[2], o[3]);
-        uint2 pk;
-        pk.x = *reinterpret_cast<uint32_t*>(&lo);
-        pk.y = *reinterpret_cast<uint32_t*>(&hi);
-        *reinterpret_cast<uint2*>(out + (r0 + r) * d + c0) = pk;
-    }
-}
-
 __global__ void gather_rows_f32_kernel(const float* __restrict__ src, const int64_t* __restrict__ idx, int64_t n, int c,
                                        float* __restrict__ dst) {
     int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -905,17 +840,6 @@ int launch_gate_add_staged(__nv_bfloat16* x, const __nv_bfloat16* h, int64_t h_s
     const size_t smem = (size_t)kGaVecBytes * d + (size_t)nwarps * per_warp;
     const unsigned grid = (unsigned)std::min<int64_t>((m + nwarps - 1) / nwarps, sms[dev]);
     gate_add_modulate_staged_kernel<<<grid, nwarps * 32, smem, s>>>(x, h, h_stride, m, d, g, c2, g2, s1, sh, mod_out);
-    count_launches(1);
-    return check_launch();
-}
-
-extern "C" int vdit_patchify(const float* xt, int64_t n, const float* w, int32_t d, void* x_out, vdit_stream_t stream) {
-    if (n < 0 || d <= 0 || d % 8 || !xt || !w || !x_out) return VDIT_ERR_ARG;
-    if (!aligned16(xt) || !aligned16(w) || !aligned16(x_out)) return VDIT_ERR_ALIGN;
-    if (n == 0) return VDIT_OK;
-    if (d % 2) return VDIT_ERR_UNSUPPORTED;
-    patchify_kernel<<<dim3((d + kPatchCols - 1) / kPatchCols, (unsigned)((n + kPatchRows - 1) / kPatchRows)), 256, 0,
-                      static_cast<cudaStream_t>(stream)>>>(xt, n, w, d, static_cast<__nv_bfloat16*>(x_out));
     count_launches(1);
     return check_launch();
 }

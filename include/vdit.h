@@ -84,7 +84,8 @@ int vdit_rope2d_table(int32_t cond_size, int32_t head_dim, double base, float* c
                       float* sin_out, vdit_stream_t stream);
 
 /* ------------------------------------------------------------------ row kernels */
-/* x[n,d] bf16 = xt[n,16] fp32 @ w[d,16]^T (patchify, lib/fast_flow.py:931-935). */
+/* x[n,d] bf16 = xt[n,16] fp32 @ w[d,16]^T (patchify, lib/fast_flow.py:931-935); xt, w, x 16-byte
+ * aligned, d % 8 == 0, n < 2^31 (else VDIT_ERR_UNSUPPORTED). */
 int vdit_patchify(const float* xt, int64_t n, const float* w, int32_t d, void* x_out,
                   vdit_stream_t stream);
 
