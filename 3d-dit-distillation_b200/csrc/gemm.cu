@@ -16,7 +16,9 @@
 //               commits arrive on the stage / accumulator barriers of both CTAs
 //   warps 2..5  epilogue: warp w drains TMEM lane quarter w % 4 (32 of the CTA's 128
 //               rows) while the MMAs of the next tile run into the other accumulator,
-//               then arrives on the even CTA's accumulator-free barrier
+//               then arrives on the even CTA's accumulator-free barrier; the qkv epilogue
+//               (QK-norm, RoPE, scatter) has eight warps, 2..9, warp w taking head
+//               (w - 2) / 4 of the tile's two heads in lane quarter w % 4
 // Every mbarrier wait is bounded; a wait that runs out records an error in
 // g_gemm_error, raises the CTA abort flag and the CTA skips to its teardown (cluster
 // barrier, TMEM always freed).
@@ -37,8 +39,7 @@ using namespace tc;
 
 constexpr int BM = 128;             // rows per CTA (256 per pair)
 constexpr int BK = 64;
-constexpr int EPI_WARPS = 4;
-constexpr int THREADS = (2 + EPI_WARPS) * 32;
+constexpr int EPI_WARPS = 4;                   // bias epilogue (the qkv epilogue has 8)
 constexpr int kErr = 0x474D;   // "GM": a bounded wait of the GEMM kernel ran out
 
 // epilogue kinds
@@ -48,15 +49,15 @@ constexpr int EPI_QKV = 1;    // self-attention qkv: QK-RMSNorm + 3D RoPE, rows 
 constexpr int kQkvTableBytes = 24576;   // EPI_QKV: RoPE cos + sin tables staged in shared memory
 
 // EPI_BIAS: a 6-stage ring (8 for 128-column tiles) and, per epilogue warp, two 32-row x 64-column bf16 boxes stored
-// by TMA.  EPI_QKV: a 4-stage ring, the RoPE tables and, per epilogue warp, two buffers of
-// 32 head rows (one per head of the tile), padded to spread the lanes' stores over the
-// banks; each row leaves with its own bulk copy to its scattered output row.
+// by TMA.  EPI_QKV: a 4-stage ring, the RoPE tables and, per epilogue warp (eight, one head
+// each), one buffer of 32 head rows, padded to spread the lanes' stores over the banks; each
+// row leaves with its own bulk copy to its scattered output row.
 template <int EPI, int BN>
 struct __align__(1024) Smem {
     static constexpr int NST = EPI == EPI_QKV ? 4 : BN == 128 ? 8 : 6;
     static constexpr int ROWPAD = BN + 16;                 // a head row: BN / 2 bf16 = BN bytes
     static constexpr int XBYTES =
-        EPI == EPI_QKV ? kQkvTableBytes + EPI_WARPS * 2 * 32 * ROWPAD : EPI_WARPS * 2 * 32 * 128;
+        EPI == EPI_QKV ? kQkvTableBytes + 8 * 32 * ROWPAD : EPI_WARPS * 2 * 32 * 128;
     uint8_t a[NST][BM * 128];
     uint8_t b[NST][BN / 2 * 128];    // this CTA's half of the weight tile
     uint8_t x[XBYTES];
@@ -97,8 +98,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
                  : "memory");
 }
 
+// epilogue warps and threads of a kernel kind
+template <int EPI>
+__host__ __device__ constexpr int epi_warps() { return EPI == EPI_QKV ? 8 : EPI_WARPS; }
+template <int EPI>
+__host__ __device__ constexpr int threads_of() { return (2 + epi_warps<EPI>()) * 32; }
+
 template <int EPI, int BN>
-__global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+__global__ void __launch_bounds__(threads_of<EPI>(), 1) gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                           const __grid_constant__ CUtensorMap tmW,
                                                           const __grid_constant__ CUtensorMap tmO, int64_t m, int n,
                                                           int k, const __grid_constant__ EpiArgs ep) {
@@ -128,7 +135,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(smem_u32(&sm.acc_full[b]), 1);
-            mbar_init(smem_u32(&sm.acc_empty[b]), 2 * EPI_WARPS);
+            mbar_init(smem_u32(&sm.acc_empty[b]), 2 * epi_warps<EPI>());
         }
         sm.abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -139,7 +146,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
     if (EPI == EPI_QKV) {   // RoPE tables into the staging area (this epilogue stores from registers)
         float* tab = reinterpret_cast<float*>(sm.x);
         const int nt = ep.res * kQkvM;
-        for (int i = threadIdx.x; i < nt; i += THREADS) {
+        for (int i = threadIdx.x; i < nt; i += threads_of<EPI>()) {
             tab[i] = __ldg(ep.cos_t + i);
             tab[nt + i] = __ldg(ep.sin_t + i);
         }
@@ -285,8 +292,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
                 }
                 const float* cs_s = reinterpret_cast<const float*>(sm.x);
                 const float* sn_s = cs_s + ep.res * kQkvM;
-#pragma unroll 1
-                for (int hh = 0; hh < BN / kQkvHd; ++hh) {
+                {
+                    const int hh = ew >> 2;                     // this warp's head of the tile
                     const int col = col0 + hh * kQkvHd;
                     const int section = col / ep.d;                 // 0 q, 1 k, 2 v
                     float x[kQkvHd];
@@ -327,10 +334,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
                             }
                         }
                     }
-                    // the row into this head's buffer (free once the previous tile's copy of it has
-                    // been read), then one bulk copy of its kQkvHd * 2 bytes to the scattered row
-                    uint8_t* rb = sm.x + kQkvTableBytes + ((ew * 2 + hh) * 32 + lane) * SM::ROWPAD;
-                    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                    // the row into the warp's buffer (free once the previous tile's copy has been
+                    // read), then one bulk copy of its kQkvHd * 2 bytes to the scattered row
+                    uint8_t* rb = sm.x + kQkvTableBytes + (ew * 32 + lane) * SM::ROWPAD;
+                    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 #pragma unroll
                     for (int q = 0; q < kQkvHd / 8; ++q) *reinterpret_cast<uint4*>(rb + q * 16) = pack8(x + q * 8);
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -389,7 +396,7 @@ cudaLaunchConfig_t launch_config(cudaLaunchAttribute* attr, cudaStream_t s) {
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(THREADS);
+    cfg.blockDim = dim3(threads_of<EPI>());
     cfg.dynamicSmemBytes = sizeof(Smem<EPI, BN>) + 1024;
     cfg.stream = s;
     cfg.attrs = attr;
