@@ -150,6 +150,7 @@ __global__ void __launch_bounds__(256) gate_add_modulate_kernel(
 // copies are bounded; a timeout sets the row kernels' error word.
 constexpr int kGaMaxWarps = 16;
 constexpr int kGaVecBytes = 20;          // shared fp32 vectors per column: g, s1, sh, g2, c2
+constexpr int kGaSlots = 4;              // row slots per warp (an even number)
 constexpr int kErrRowTimeout = 0x524f;   // "RO": a bounded wait of a row kernel ran out
 
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
@@ -174,11 +175,12 @@ __global__ void __launch_bounds__(kGaMaxWarps * 32, 1) gate_add_modulate_staged_
     float* pg2 = psh + d;            // second residual: its gate and its (broadcast) row in fp32
     float* pc2 = pg2 + d;
     const uint32_t row_bytes = 2u * (uint32_t)d;
-    // a warp's four row slots: two stages of [x | h] with the residual, else four stages of x
-    const int nst = add ? 2 : 4;
-    uint8_t* wbuf = smem + (size_t)kGaVecBytes * d + (size_t)warp * 4 * row_bytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kGaVecBytes * d + (size_t)nwarps * 4 * row_bytes) +
-                     warp * 4;
+    // a warp's row slots: stages of [x | h] with the residual, else stages of x alone
+    const int nst = add ? kGaSlots / 2 : kGaSlots;
+    uint8_t* wbuf = smem + (size_t)kGaVecBytes * d + (size_t)warp * kGaSlots * row_bytes;
+    uint64_t* bars =
+        reinterpret_cast<uint64_t*>(smem + (size_t)kGaVecBytes * d + (size_t)nwarps * kGaSlots * row_bytes) +
+        warp * kGaSlots;
     const uint32_t bar0 = tc::smem_u32(bars);
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
         if (add) pg[i] = g[i];
@@ -823,7 +825,7 @@ int launch_gate_add_staged(__nv_bfloat16* x, const __nv_bfloat16* h, int64_t h_s
         return VDIT_ERR_LAUNCH;
     }
     constexpr size_t kMaxSmem = 227 * 1024 - 256;
-    const size_t per_warp = (size_t)8 * d + 32;         // four row slots and four barriers
+    const size_t per_warp = (size_t)kGaSlots * (2 * d + 8);   // row slots and their barriers
     const int nwarps = (int)std::min<size_t>(kGaMaxWarps, (kMaxSmem - (size_t)kGaVecBytes * d) / per_warp);
     if (sms[dev] == 0) {
         int n = 0;
