@@ -445,13 +445,31 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo, 
     return check_launch();
 }
 
-// The pair tile width for an [m, n] output: the widest of 256, 192 and 128 columns that
-// divides n (128, with a partial last tile, when none does).  The mainloop is bound by shared-memory bandwidth (MMA operand reads plus TMA
-// fills: 128, 146 and 190 bytes per clock at the full MMA rate for those widths), so per
-// FLOP a 192-column tile runs 1.17x and a 128-column tile 1.5x the time of a 256-column
-// one, more than a narrower tile ever saves on a partial last round.
-int pick_bn(int n) {
-    return n % 256 == 0 ? 256 : n % 192 == 0 ? 192 : 128;
+// The pair tile width for an [m, n] output, among 256, 192 and 128 columns that divide n
+// (128, with a partial last tile, when none does): the one with the least estimated time,
+// rounds of tiles over the resident CTA pairs x the time of one tile.  The mainloop is
+// bound by shared-memory bandwidth (MMA operand reads plus TMA fills: 128, 146 and 190
+// bytes per clock at the full MMA rate for those widths), so a 192-column tile takes
+// 0.75 x 1.17 and a 128-column tile 0.5 x 1.5 of a 256-column tile's time.  The 4101-row
+// context linears with n = 1536 come out at 192 (17 x 8 tiles in two rounds of 74 pairs
+// instead of 17 x 6 in a second round 38% full); every 16384-row shape keeps 256.
+int pick_bn(int64_t m, int n) {
+    const int64_t tiles_m = (m + 2 * BM - 1) / (2 * BM);
+    const int64_t pairs = std::max(1, num_sms() / 2);
+    const int widths[3] = {256, 192, 128};
+    const double cost[3] = {1.0, 0.75 * 1.17, 0.5 * 1.5};
+    int best = 128;
+    double best_t = 1e300;
+    for (int i = 0; i < 3; ++i) {
+        if (n % widths[i]) continue;
+        const int64_t tiles = tiles_m * (n / widths[i]);
+        const double t = (double)((tiles + pairs - 1) / pairs) * cost[i];
+        if (t < best_t) {
+            best_t = t;
+            best = widths[i];
+        }
+    }
+    return best;
 }
 
 }  // namespace gemm
@@ -481,7 +499,7 @@ extern "C" int vdit_linear(const void* a, int64_t lda, const void* w, int64_t ld
         return VDIT_ERR_ALIGN;
     if (m == 0) return VDIT_OK;
     if (m > (int64_t)INT32_MAX) return VDIT_ERR_UNSUPPORTED;
-    const int bn = pick_bn(n);
+    const int bn = pick_bn(m, n);
     CUtensorMap ma, mw, mo;
     if (!make_map(&ma, a, m, k, lda, BM) || !make_map(&mw, w, n, k, ldw, bn / 2) || !make_map(&mo, out, m, n, ldo, 32, 64))
         return VDIT_ERR_DRIVER;
