@@ -22,7 +22,7 @@ namespace {
 constexpr int kRows = 8;               // rows per batch of the streaming pass
 constexpr int kHg = 4;                 // heads per block (kRows * kHg = 32 partial scores per thread)
 constexpr int kMaxHeads = 16;
-constexpr int kRowsPerRange = 128;
+constexpr int kMinRowsPerRange = 64;   // shortest row range of the streaming pass
 constexpr int kFoldThreads = 256;
 constexpr int kCombThreads = 256;
 
@@ -253,8 +253,22 @@ __global__ void __launch_bounds__(kCombThreads) wide1q_project_kernel(const floa
     if (lane == 0) out[o] = f2bf(acc + bf2f(bv[o]));
 }
 
-int splits_for(int64_t n) {      // row ranges (the combine kernel merges at most 1024)
-    return (int)std::max<int64_t>(1, std::min<int64_t>(1024, (n + kRowsPerRange - 1) / kRowsPerRange));
+// Row ranges of the streaming pass: one wave of CTAs (ranges x head groups = the SM count, one
+// CTA per SM) unless the ranges would get shorter than kMinRowsPerRange rows.  At n = 16384,
+// 12 heads: 49 ranges of 335 rows, 147 CTAs, against 128 ranges of 128 rows in 2.6 waves, which
+// measured 7% slower (and 64 ranges of 256 rows in 1.3 waves 17% slower).  The merge kernel takes
+// at most 1024 ranges.
+int splits_for(int64_t n, int heads) {
+    static int sms = 0;
+    if (sms == 0) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            sms = 148;
+    }
+    const int ngroups = std::max(1, (heads + kHg - 1) / kHg);
+    const int64_t wave = std::max(1, sms / ngroups);
+    const int64_t most = (n + kMinRowsPerRange - 1) / kMinRowsPerRange;
+    return (int)std::max<int64_t>(1, std::min<int64_t>(1024, std::min(wave, most)));
 }
 
 }  // namespace
@@ -264,7 +278,7 @@ using namespace vdit;
 
 extern "C" size_t vdit_attention_1q_wide_workspace_bytes(int32_t heads, int32_t head_dim, int64_t n_keys) {
     const int64_t d = (int64_t)heads * head_dim;
-    return (size_t)heads * (size_t)(d + 2) * sizeof(float) * (size_t)(2 + splits_for(n_keys));
+    return (size_t)heads * (size_t)(d + 2) * sizeof(float) * (size_t)(2 + splits_for(n_keys, heads));
 }
 
 extern "C" int vdit_attention_1q_wide(const void* q, const void* x, int64_t ldx, int64_t n, const void* wk,
@@ -277,7 +291,7 @@ extern "C" int vdit_attention_1q_wide(const void* q, const void* x, int64_t ldx,
     if (ldx < d || ldw < d) return VDIT_ERR_ARG;
     if (!aligned16(x) || !aligned16(wv) || !aligned16(workspace) || ldx % 8 || ldw % 8) return VDIT_ERR_ALIGN;
     if (workspace_bytes < vdit_attention_1q_wide_workspace_bytes(heads, head_dim, n)) return VDIT_ERR_WORKSPACE;
-    const int splits = splits_for(n);
+    const int splits = splits_for(n, heads);
     float* qf = static_cast<float*>(workspace);  // heads x d, then ubar heads x d, then splits x heads x (d + 2)
     float* ubar = qf + heads * d;
     float* ws = ubar + heads * d;
