@@ -103,6 +103,8 @@ class OptimizedLatDitRunner:
         # event, algorithmic units, whether another NFE shared the GPU) under its kernel
         # class (KERNEL_CLASSES): the benchmark's in-step measurement of each kernel
         self.kernel_timer: Optional[Dict[str, list]] = None
+        # when a set, only these kernel classes are timed (the others launch without events)
+        self.kernel_timer_kinds: Optional[set] = None
         self._nfe_shared = False
         self._ctx_rows = -1            # rows of the context stream in the current NFE (GEMM classes)
         # the context stream of the context blocks runs on its own CUDA stream
@@ -220,7 +222,7 @@ class OptimizedLatDitRunner:
         """fn(*args, **kw); with the kernel timer on, CUDA events around it on the current
         stream, filed under ``kind`` with its algorithmic units (FLOPs or bytes)."""
         kt = self.kernel_timer
-        if kt is None:
+        if kt is None or (self.kernel_timer_kinds is not None and kind not in self.kernel_timer_kinds):
             return fn(*args, **kw)
         e0 = torch.cuda.Event(enable_timing=True)
         e0.record()

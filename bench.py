@@ -731,9 +731,9 @@ def kernel_table(timer: dict, hbm_peak: float, tensor_peak: float, peak_kind: st
     """Per kernel class: launches, average CUDA-event duration, algorithmic FLOPs or bytes
     per launch and the fraction of the measured peak (sustained bf16 GEMM rate for
     tensor-core classes, HBM copy bandwidth for byte-bound ones).  `timer` holds the launches
-    inside the timed steps, where a guided step runs its two NFEs on two streams that share
-    the GPU; `solo`, when given, the same classes from one NFE of each branch with every kernel
-    alone on the GPU (`solo_ms_per_launch`, `solo_frac`)."""
+    of one whole sample run right after the timed steps, where a guided step runs its two NFEs
+    on two streams that share the GPU; `solo`, when given, the same classes from one NFE of
+    each branch with every kernel alone on the GPU (`solo_ms_per_launch`, `solo_frac`)."""
     from vdit.fast_flow import KERNEL_CLASSES
 
     def rate(kind, ev):
@@ -893,7 +893,10 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     ktimer: dict = {}
-    runner.kernel_timer = ktimer                 # the main kernels' launches inside the timed steps
+    # inside the timed steps only the dominant kernel (window self-attention) is bracketed by
+    # CUDA events; the other ~1700 launches of a sample run without them
+    runner.kernel_timer = ktimer
+    runner.kernel_timer_kinds = {"attention_window_self"}
     with ClockSampler(local) as clk:
         for i in range(args.steps):
             _l2_flush(flush)
@@ -902,7 +905,16 @@ def main():
             evs[i][1].record(s)
         torch.cuda.synchronize()
     runner.kernel_timer = None
+    runner.kernel_timer_kinds = None
     launches = (_lib.launch_count() - launches0) // max(args.steps, 1)
+    # every kernel class of the forward, in one more sample after the timed steps (not timed
+    # as a step): CUDA events around each launch on its stream
+    kstep: dict = {}
+    _l2_flush(flush)
+    runner.kernel_timer = kstep
+    step()
+    torch.cuda.synchronize()
+    runner.kernel_timer = None
     total_ms = sum(a.elapsed_time(b) for a, b in evs)
     t = torch.tensor([total_ms], device=dev)
     if dist is not None:
@@ -986,7 +998,7 @@ def main():
     solo_ms = statistics.fmean(a.elapsed_time(b) for a, b in solo) if solo else None
     flops_alone, att_ms_alone = attention_roofline(w, runner)
     traffic = attention_traffic()
-    kernels = kernel_table(ktimer, hbm, tflops_sustained, peak_kind, solo=ksolo)
+    kernels = kernel_table(kstep, hbm, tflops_sustained, peak_kind, solo=ksolo)
     assert _lib.device_error() == 0, "device error word set during the benchmark"
 
     # ---------------------------------------------------------------- C5 sharded batch (strong scaling)
@@ -1028,6 +1040,9 @@ def main():
                          "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of "
                                            "the same kernel source (profiles/attention_traffic.json)",
                          "kernels": kernels,
+                         "kernels_source": "one sample run right after the timed steps with CUDA events around "
+                                           "every launch (the timed steps carry events around the window "
+                                           "self-attention launches only)",
                          "unshared": None if solo_ms is None else {
                              "ms_per_launch": solo_ms, "launches": len(solo),
                              "achieved": flops / (solo_ms / 1e3) / 1e12,
