@@ -109,30 +109,48 @@ def _l2_flush(buf: torch.Tensor):
     buf.add_(1)          # 256 MiB write: larger than the 126 MB L2
 
 
+CPU_SAMPLE = ("CPU oracle (fp32) at N=16384, L=4101, 12x128: one context block and one plain block of the "
+              "conditional NFE and the same two of the exact 1-token NFE, each run once; the 7-NFE sample "
+              "(4 conditional + 3 1-token NFEs, each 8 context + 16 plain blocks) extrapolated from them")
+
+
 def cpu_baseline_sample(threads: int):
-    """The CPU oracle (fp32) on one non-context transformer block of the same workload
-    (N=16384, L=4101, 12x128 heads); per-NFE time extrapolated x24 blocks."""
+    """The CPU oracle (fp32) on the same workload (N=16384 shell voxels, L=4101 context tokens,
+    12x128 heads): one context block (0) and one plain block (8) of the conditional NFE and the
+    same two blocks of the exact 1-token NFE, each run once.  A 7-NFE sample is extrapolated as
+    4 x (8 context + 16 plain blocks) + 3 x (8 + 16 blocks of the 1-token branch), the GPU arm's
+    mix.  Returns (voxel-tokens/s per NFE, seconds of CPU work)."""
     from oracle import model as om
     from vdit.workloads import C4, shell_voxels
     torch.set_num_threads(threads)
     w = C4()
-    cfg = om.ModelConfig(dim=1536, head_dim=128, depth=9, cond_depth=8, res=64)
+    D = 1536
+    cfg = om.ModelConfig(dim=D, head_dim=128, depth=9, cond_depth=8, res=64)
     shapes = om.param_shapes(cfg)
     g = torch.Generator().manual_seed(0)
     p = {k: (torch.ones(v) if k.endswith("_scale") or k == "std" else torch.randn(v, generator=g) * 0.02)
-         for k, v in shapes.items() if "blocks.8." in k}
+         for k, v in shapes.items() if ("blocks.0." in k or "blocks.8." in k) and "gates" not in k}
     vox = shell_voxels(w.n, w.grid, w.radius, 0)
     geom = om.build_geometry(vox, cfg)
-    x = torch.randn(w.n, 1536, generator=g)
-    c = torch.randn(w.ctx_tokens, 1536, generator=g)
+    x = torch.randn(w.n, D, generator=g)
+    c = torch.randn(w.ctx_tokens, D, generator=g)
+    c1 = torch.randn(1, D, generator=g)
+    cpos = om.cond_positions(w.ctx_tokens)
     gates = {"blocks": [None] * 9, "cond": [None] * 9}
-    gates["blocks"][8] = torch.randn(9, 1536, generator=g) * 0.1
-    gates["cond"][8] = torch.randn(2, 1536, generator=g) * 0.1
-    t0 = time.perf_counter()
+    for b, nc in ((0, 9), (8, 2)):
+        gates["blocks"][b] = torch.randn(9, D, generator=g) * 0.1
+        gates["cond"][b] = torch.randn(nc, D, generator=g) * 0.1
+    t = {}
     with torch.no_grad():
-        om.block_forward(p, cfg, 8, x, c, gates, geom, None)
-    dt = time.perf_counter() - t0
-    return w.n / (dt * 24), dt
+        for name, fn in (("ctx", lambda: om.block_forward(p, cfg, 0, x, c, gates, geom, cpos)),
+                         ("plain", lambda: om.block_forward(p, cfg, 8, x, c, gates, geom, None)),
+                         ("ctx_1tok", lambda: om.block_forward_1tok(p, cfg, 0, x, c1, None, gates, geom)),
+                         ("plain_1tok", lambda: om.block_forward_1tok(p, cfg, 8, x, c1, None, gates, geom))):
+            t0 = time.perf_counter()
+            fn()
+            t[name] = time.perf_counter() - t0
+    t_sample = 4 * (8 * t["ctx"] + 16 * t["plain"]) + 3 * (8 * t["ctx_1tok"] + 16 * t["plain_1tok"])
+    return NFE_PER_SAMPLE * w.n / t_sample, sum(t.values())
 
 
 def run_reference(args):
@@ -151,8 +169,7 @@ def run_reference(args):
         vals.append(v)
         times.append(dt)
     value = float(statistics.median(vals))
-    sample = ("one non-context block (of 24) of the pos NFE at N=16384, L=4101, 12x128, fp32, "
-              "extrapolated x24 blocks per NFE (context blocks cost ~2x, so this overstates CPU throughput)")
+    sample = CPU_SAMPLE
     from vdit.workloads import C4
     w = C4()
     print(json.dumps({
@@ -1013,8 +1030,7 @@ def main():
         threads = os.cpu_count() or 1
         v, dt = cpu_baseline_sample(threads)
         cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"CPU oracle (fp32) on one non-context block of the pos NFE at N=16384, L=4101 "
-                         f"({dt:.1f} s), extrapolated x24 blocks per NFE"}
+               "sample": f"{CPU_SAMPLE} ({dt:.1f} s)"}
 
     if rank == 0:
         print(json.dumps({

@@ -326,55 +326,65 @@ def flow_forward(p: Params, cfg: ModelConfig, xt_sorted: torch.Tensor, t_val: fl
     return F.linear(modulate(x, o_s, o_sh), p["flow.unpatchify.weight"])
 
 
+def block_forward_1tok(p: Params, cfg: ModelConfig, b: int, x: torch.Tensor, c: torch.Tensor,
+                       ln_c: Optional[torch.Tensor], gates: dict, geom: Geometry):
+    """One block of the exact 1-token zero-context branch (``lib/fast_flow.py:1702-1794`` for
+    the context blocks, ``:2295-2309`` for the others).  ``c`` is the single context token
+    [1,D]; ``ln_c`` its LayerNorm after the last context block (None until a plain block
+    computes it).  Returns (x, c, ln_c)."""
+    H, HD, D = cfg.heads, cfg.head_dim, cfg.dim
+    N = x.shape[0]
+    pre = f"flow.blocks.{b}."
+    s_msa, sh_msa, g_msa, s_cr, sh_cr, g_cr, s_mlp, sh_mlp, g_mlp = gates["blocks"][b]
+    qkv = linear(p, pre + "to_qkv", modulate(x, s_msa, sh_msa)).view(N, 3, H, HD)
+    q, k = _qknorm(p, pre + "qk_norm.", qkv[:, 0], qkv[:, 1])
+    q, k = rope_nd(q, geom.pos3, 128.0), rope_nd(k, geom.pos3, 128.0)
+    fwd, bwd = geom.orders[b % len(geom.orders)]
+    qs, ks, vs = q[fwd], k[fwd], qkv[:, 2][fwd]
+    o = torch.empty_like(qs)
+    cu = geom.cu_seqlens
+    for i in range(len(cu) - 1):
+        o[cu[i]:cu[i + 1]] = attention(qs[cu[i]:cu[i + 1]], ks[cu[i]:cu[i + 1]], vs[cu[i]:cu[i + 1]])
+    x = x + linear(p, pre + "to_out", o[bwd].reshape(N, D)) * g_msa
+    if b < cfg.cond_depth:
+        cs_msa, csh_msa, cg_msa, cs_cr, csh_cr, cg_cr, cs_mlp, csh_mlp, cg_mlp = gates["cond"][b]
+        vcs = linear(p, pre + "cond_to_qkv", modulate(c, cs_msa, csh_msa))[:, 2 * D:]
+        c = c + linear(p, pre + "cond_to_out", vcs) * cg_msa
+        qkvc = linear(p, pre + "cond_to_qkv_cross", modulate(c, cs_cr, csh_cr))
+        qc, vc = qkvc[:, :D].view(1, H, HD), qkvc[:, 2 * D:]
+        x_const = linear(p, pre + "to_out_cross", vc)           # attention over equal keys -> V_c
+        kv = linear(p, pre + "to_qkv_cross", modulate(x, s_cr, sh_cr))[:, D:].view(N, 2, H, HD)
+        hcx = attention(qc, kv[:, 0], kv[:, 1]).reshape(1, D)   # one query over N keys
+        x = x + x_const * g_cr
+        c = c + linear(p, pre + "cond_to_out_cross", hcx) * cg_cr
+    else:
+        if ln_c is None:
+            ln_c = layer_norm(c)
+        cs_cr, csh_cr = gates["cond"][b]
+        vc = linear(p, pre + "cond_to_kv_cross", ln_c * (1 + cs_cr) + csh_cr)[:, D:]
+        x = x + linear(p, pre + "to_out_cross", vc) * g_cr
+    h = linear(p, pre + "ffn0", modulate(x, s_mlp, sh_mlp))
+    h = dwconv27(h, p[pre + "ffn_conv.weight"], p[pre + "ffn_conv.bias"], geom.conv_indices)
+    a, g = h.chunk(2, -1)
+    x = x + linear(p, pre + "ffn1", F.silu(g) * a) * g_mlp
+    if b < cfg.cond_depth:
+        a, g = linear(p, pre + "cond_ffn0", modulate(c, cs_mlp, csh_mlp)).chunk(2, -1)
+        c = c + linear(p, pre + "cond_ffn1", F.silu(g) * a) * cg_mlp
+    return x, c, ln_c
+
+
 def flow_forward_1tok(p: Params, cfg: ModelConfig, xt_sorted: torch.Tensor, t_val: float,
                       geom: Geometry) -> torch.Tensor:
     """Exact 1-token restatement of the zero-context branch (``lib/fast_flow.py``
     ``:937-958, 1702-1794, 2295-2309``).  With an all-zero context every
     context token stays identical, so self-attention returns V, x->context
     attention returns V_c, and context->x is a single query over N keys."""
-    H, HD, D = cfg.heads, cfg.head_dim, cfg.dim
     gates = time_gates(p, cfg, t_val)
     x = F.linear(xt_sorted.float(), p["flow.patchify.weight"])
-    c = torch.zeros(1, D)
-    N = x.shape[0]
+    c = torch.zeros(1, cfg.dim)
     ln_c = None
     for b in range(cfg.depth):
-        pre = f"flow.blocks.{b}."
-        s_msa, sh_msa, g_msa, s_cr, sh_cr, g_cr, s_mlp, sh_mlp, g_mlp = gates["blocks"][b]
-        qkv = linear(p, pre + "to_qkv", modulate(x, s_msa, sh_msa)).view(N, 3, H, HD)
-        q, k = _qknorm(p, pre + "qk_norm.", qkv[:, 0], qkv[:, 1])
-        q, k = rope_nd(q, geom.pos3, 128.0), rope_nd(k, geom.pos3, 128.0)
-        fwd, bwd = geom.orders[b % len(geom.orders)]
-        qs, ks, vs = q[fwd], k[fwd], qkv[:, 2][fwd]
-        o = torch.empty_like(qs)
-        cu = geom.cu_seqlens
-        for i in range(len(cu) - 1):
-            o[cu[i]:cu[i + 1]] = attention(qs[cu[i]:cu[i + 1]], ks[cu[i]:cu[i + 1]], vs[cu[i]:cu[i + 1]])
-        x = x + linear(p, pre + "to_out", o[bwd].reshape(N, D)) * g_msa
-        if b < cfg.cond_depth:
-            cs_msa, csh_msa, cg_msa, cs_cr, csh_cr, cg_cr, cs_mlp, csh_mlp, cg_mlp = gates["cond"][b]
-            vcs = linear(p, pre + "cond_to_qkv", modulate(c, cs_msa, csh_msa))[:, 2 * D:]
-            c = c + linear(p, pre + "cond_to_out", vcs) * cg_msa
-            qkvc = linear(p, pre + "cond_to_qkv_cross", modulate(c, cs_cr, csh_cr))
-            qc, vc = qkvc[:, :D].view(1, H, HD), qkvc[:, 2 * D:]
-            x_const = linear(p, pre + "to_out_cross", vc)           # attention over equal keys -> V_c
-            kv = linear(p, pre + "to_qkv_cross", modulate(x, s_cr, sh_cr))[:, D:].view(N, 2, H, HD)
-            hcx = attention(qc, kv[:, 0], kv[:, 1]).reshape(1, D)   # one query over N keys
-            x = x + x_const * g_cr
-            c = c + linear(p, pre + "cond_to_out_cross", hcx) * cg_cr
-        else:
-            if ln_c is None:
-                ln_c = layer_norm(c)
-            cs_cr, csh_cr = gates["cond"][b]
-            vc = linear(p, pre + "cond_to_kv_cross", ln_c * (1 + cs_cr) + csh_cr)[:, D:]
-            x = x + linear(p, pre + "to_out_cross", vc) * g_cr
-        h = linear(p, pre + "ffn0", modulate(x, s_mlp, sh_mlp))
-        h = dwconv27(h, p[pre + "ffn_conv.weight"], p[pre + "ffn_conv.bias"], geom.conv_indices)
-        a, g = h.chunk(2, -1)
-        x = x + linear(p, pre + "ffn1", F.silu(g) * a) * g_mlp
-        if b < cfg.cond_depth:
-            a, g = linear(p, pre + "cond_ffn0", modulate(c, cs_mlp, csh_mlp)).chunk(2, -1)
-            c = c + linear(p, pre + "cond_ffn1", F.silu(g) * a) * cg_mlp
+        x, c, ln_c = block_forward_1tok(p, cfg, b, x, c, ln_c, gates, geom)
     o_s, o_sh = gates["out"]
     return F.linear(modulate(x, o_s, o_sh), p["flow.unpatchify.weight"])
 

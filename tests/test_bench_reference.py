@@ -1,5 +1,5 @@
 """The reference arm of ``bench.py`` (the oracle port on the host CPU) runs end to end
-and prints the contract line.  The block forward itself is replaced by a stub here so
+and prints the contract line.  The block forwards themselves are replaced by stubs here so
 the test takes seconds; everything around it (imports, the workload's voxel set and
 geometry, the line's keys) is the real code path."""
 import json
@@ -14,6 +14,7 @@ def test_reference_arm_prints_contract_line(monkeypatch, capsys):
     import bench
     from oracle import model as om
     monkeypatch.setattr(om, "block_forward", lambda *a, **k: None)
+    monkeypatch.setattr(om, "block_forward_1tok", lambda *a, **k: None)
 
     class Args:
         steps, warmup, gpus = 1, 0, 1
