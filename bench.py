@@ -110,74 +110,97 @@ def _l2_flush(buf: torch.Tensor):
 
 
 CPU_SAMPLE = ("CPU oracle (fp32) at N=16384, L=4101, 12x128: one context block and one plain block of the "
-              "conditional NFE and the same two of the exact 1-token NFE, each run once; the 7-NFE sample "
-              "(4 conditional + 3 1-token NFEs, each 8 context + 16 plain blocks) extrapolated from them")
+              "conditional NFE and the same two of the exact 1-token NFE; the 7-NFE sample (4 conditional + "
+              "3 1-token NFEs, each 8 context + 16 plain blocks) extrapolated from their times")
+CPU_BLOCK_KINDS = ("ctx", "plain", "ctx_1tok", "plain_1tok")
+
+
+class CpuBlocks:
+    """The CPU oracle (fp32) on the workload's shapes (N=16384 shell voxels, L=4101 context
+    tokens, 12x128 heads): weights of one context block (0) and one plain block (8), the
+    voxel set's geometry and the inputs are built once; ``run(kind)`` times one block of the
+    conditional NFE ("ctx", "plain") or of the exact 1-token NFE ("ctx_1tok", "plain_1tok")."""
+
+    def __init__(self, threads: int):
+        from oracle import model as om
+        from vdit.workloads import C4, shell_voxels
+        torch.set_num_threads(threads)
+        self.om, self.w, D = om, C4(), 1536
+        self.cfg = om.ModelConfig(dim=D, head_dim=128, depth=9, cond_depth=8, res=64)
+        g = torch.Generator().manual_seed(0)
+        self.p = {k: (torch.ones(v) if k.endswith("_scale") or k == "std" else torch.randn(v, generator=g) * 0.02)
+                  for k, v in om.param_shapes(self.cfg).items()
+                  if ("blocks.0." in k or "blocks.8." in k) and "gates" not in k}
+        self.geom = om.build_geometry(shell_voxels(self.w.n, self.w.grid, self.w.radius, 0), self.cfg)
+        self.x = torch.randn(self.w.n, D, generator=g)
+        self.c = torch.randn(self.w.ctx_tokens, D, generator=g)
+        self.c1 = torch.randn(1, D, generator=g)
+        self.cpos = om.cond_positions(self.w.ctx_tokens)
+        self.gates = {"blocks": [None] * 9, "cond": [None] * 9}
+        for b, nc in ((0, 9), (8, 2)):
+            self.gates["blocks"][b] = torch.randn(9, D, generator=g) * 0.1
+            self.gates["cond"][b] = torch.randn(nc, D, generator=g) * 0.1
+
+    def run(self, kind: str) -> float:
+        om, p, cfg, x, gates, geom = self.om, self.p, self.cfg, self.x, self.gates, self.geom
+        fn = {"ctx": lambda: om.block_forward(p, cfg, 0, x, self.c, gates, geom, self.cpos),
+              "plain": lambda: om.block_forward(p, cfg, 8, x, self.c, gates, geom, None),
+              "ctx_1tok": lambda: om.block_forward_1tok(p, cfg, 0, x, self.c1, None, gates, geom),
+              "plain_1tok": lambda: om.block_forward_1tok(p, cfg, 8, x, self.c1, None, gates, geom)}[kind]
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            fn()
+        return time.perf_counter() - t0
+
+    def value(self, t: dict) -> float:
+        """Voxel-tokens/s per NFE of a 7-NFE sample from the block times ``t`` (seconds per
+        kind): 4 x (8 context + 16 plain blocks) + 3 x (8 + 16 blocks of the 1-token branch),
+        the GPU arm's mix."""
+        t_sample = 4 * (8 * t["ctx"] + 16 * t["plain"]) + 3 * (8 * t["ctx_1tok"] + 16 * t["plain_1tok"])
+        return NFE_PER_SAMPLE * self.w.n / t_sample
 
 
 def cpu_baseline_sample(threads: int):
-    """The CPU oracle (fp32) on the same workload (N=16384 shell voxels, L=4101 context tokens,
-    12x128 heads): one context block (0) and one plain block (8) of the conditional NFE and the
-    same two blocks of the exact 1-token NFE, each run once.  A 7-NFE sample is extrapolated as
-    4 x (8 context + 16 plain blocks) + 3 x (8 + 16 blocks of the 1-token branch), the GPU arm's
-    mix.  Returns (voxel-tokens/s per NFE, seconds of CPU work)."""
-    from oracle import model as om
-    from vdit.workloads import C4, shell_voxels
-    torch.set_num_threads(threads)
-    w = C4()
-    D = 1536
-    cfg = om.ModelConfig(dim=D, head_dim=128, depth=9, cond_depth=8, res=64)
-    shapes = om.param_shapes(cfg)
-    g = torch.Generator().manual_seed(0)
-    p = {k: (torch.ones(v) if k.endswith("_scale") or k == "std" else torch.randn(v, generator=g) * 0.02)
-         for k, v in shapes.items() if ("blocks.0." in k or "blocks.8." in k) and "gates" not in k}
-    vox = shell_voxels(w.n, w.grid, w.radius, 0)
-    geom = om.build_geometry(vox, cfg)
-    x = torch.randn(w.n, D, generator=g)
-    c = torch.randn(w.ctx_tokens, D, generator=g)
-    c1 = torch.randn(1, D, generator=g)
-    cpos = om.cond_positions(w.ctx_tokens)
-    gates = {"blocks": [None] * 9, "cond": [None] * 9}
-    for b, nc in ((0, 9), (8, 2)):
-        gates["blocks"][b] = torch.randn(9, D, generator=g) * 0.1
-        gates["cond"][b] = torch.randn(nc, D, generator=g) * 0.1
-    t = {}
-    with torch.no_grad():
-        for name, fn in (("ctx", lambda: om.block_forward(p, cfg, 0, x, c, gates, geom, cpos)),
-                         ("plain", lambda: om.block_forward(p, cfg, 8, x, c, gates, geom, None)),
-                         ("ctx_1tok", lambda: om.block_forward_1tok(p, cfg, 0, x, c1, None, gates, geom)),
-                         ("plain_1tok", lambda: om.block_forward_1tok(p, cfg, 8, x, c1, None, gates, geom))):
-            t0 = time.perf_counter()
-            fn()
-            t[name] = time.perf_counter() - t0
-    t_sample = 4 * (8 * t["ctx"] + 16 * t["plain"]) + 3 * (8 * t["ctx_1tok"] + 16 * t["plain_1tok"])
-    return NFE_PER_SAMPLE * w.n / t_sample, sum(t.values())
+    """One CPU sample of the four block kinds, each run once.  Returns (voxel-tokens/s per
+    NFE, seconds of CPU work)."""
+    cb = CpuBlocks(threads)
+    t = {k: cb.run(k) for k in CPU_BLOCK_KINDS}
+    return cb.value(t), sum(t.values())
 
 
 def run_reference(args):
     """--impl reference: the reference algorithm on the host CPU (oracle port).  Only the
-    workload generator of the package is used (the same voxel sets as the GPU arm)."""
+    workload generator of the package is used (the same voxel sets as the GPU arm).  The
+    blocks are built once; step i times one block of kind i mod 4 (the warm-up steps run the
+    same rotation untimed), and the line's value combines the median time of each kind
+    (kinds that no timed step reached are timed once more at the end)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     load_package()
     threads = os.cpu_count() or 1
-    for _ in range(args.warmup):
-        cpu_baseline_sample(threads)
-    vals, times = [], []
-    for _ in range(args.steps):
-        v, dt = cpu_baseline_sample(threads)
-        vals.append(v)
+    cb = CpuBlocks(threads)
+    for i in range(args.warmup):
+        cb.run(CPU_BLOCK_KINDS[i % 4])
+    per_kind = {k: [] for k in CPU_BLOCK_KINDS}
+    times = []
+    for i in range(args.steps):
+        dt = cb.run(CPU_BLOCK_KINDS[i % 4])
+        per_kind[CPU_BLOCK_KINDS[i % 4]].append(dt)
         times.append(dt)
-    value = float(statistics.median(vals))
-    sample = CPU_SAMPLE
-    from vdit.workloads import C4
-    w = C4()
+    for k, v in per_kind.items():
+        if not v:
+            v.append(cb.run(k))
+    value = float(cb.value({k: statistics.median(v) for k, v in per_kind.items()}))
+    sample = CPU_SAMPLE + "; one block per step, in rotation over the four kinds"
+    w = cb.w
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "C4 full 24-block DiT, N=16384 shell r=36 in 64^3, 4101x1536 context, 12x128 heads",
                    "global_batch": 1, "seq_len": w.n},
+        "block_seconds": {k: statistics.median(v) for k, v in per_kind.items()},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
