@@ -29,3 +29,5 @@ def test_reference_arm_prints_contract_line(monkeypatch, capsys):
     assert line["e2e"] == {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
     assert line["higher_is_better"] is True and line["config"]["seq_len"] == 16384
+    # one timed step reaches the first block kind only; the other three are timed once at the end
+    assert sorted(line["block_seconds"]) == sorted(bench.CPU_BLOCK_KINDS)
