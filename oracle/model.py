@@ -158,10 +158,17 @@ def rope_nd(x: torch.Tensor, pos: torch.Tensor, base: float) -> torch.Tensor:
     return torch.cat(outs, -1)
 
 
-def attention(q, k, v):
-    """softmax(q k^T / sqrt(HD)) v on [n, H, HD] (flash-attn default scale)."""
-    s = torch.einsum("qhd,khd->hqk", q, k) / math.sqrt(q.shape[-1])
-    return torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v)
+def attention(q, k, v, score_bytes: int = 1 << 28):
+    """softmax(q k^T / sqrt(HD)) v on [n, H, HD] (flash-attn default scale).  Query rows are
+    taken in chunks whose fp32 score block stays under ``score_bytes`` (each row's softmax is
+    independent, so chunking changes no result beyond matmul rounding); without it a
+    16384 x 4101 cross-attention would hold several 3.2 GB score temporaries."""
+    nq, nk, heads = q.shape[0], k.shape[0], q.shape[1]
+    step = max(1, score_bytes // max(1, 4 * heads * nk))
+    if step >= nq:
+        s = torch.einsum("qhd,khd->hqk", q, k) / math.sqrt(q.shape[-1])
+        return torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v)
+    return torch.cat([attention(q[i:i + step], k, v, score_bytes) for i in range(0, nq, step)])
 
 
 def dwconv27(h: torch.Tensor, w: torch.Tensor, b: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
