@@ -744,7 +744,7 @@ class OptimizedLatDitRunner:
 
     @torch.no_grad()
     def warmup(self) -> None:
-        """One tiny sample so every kernel and cuBLAS handle is initialised before timing."""
+        """One tiny sample so every kernel (its attributes and tensor maps) is set up before timing."""
         vox = torch.stack(torch.meshgrid(*[torch.arange(4)] * 3, indexing="ij"), -1).reshape(-1, 3)
         dino = torch.zeros(1, 5 + 4, self.arch.dino_dim)
         self.sample_fast([vox.to(self.device)], LatDitConditioning(dino_features=dino.to(self.device)))
