@@ -177,3 +177,34 @@ def test_weights_are_bf16_detects_bf16_values():
     wb[3, 7] = wb[3, 7].nextafter(torch.tensor(float("inf")))   # one value off the bf16 grid
     assert not fk.weights_are_bf16(wb)
     assert fk.weights_are_bf16(torch.zeros(27, 8)) and fk.weights_are_bf16(torch.full((4,), -2.0 ** -130))
+
+
+def _c_kind(param: str) -> str:
+    """'ptr', 'int' or 'float' for one C parameter declaration of include/vdit.h."""
+    p = param.strip()
+    if "*" in p or p.startswith("vdit_stream_t"):
+        return "ptr"
+    if p.startswith(("float", "double")):
+        return "float"
+    return "int"
+
+
+def _py_kind(t) -> str:
+    import ctypes
+    if t in (ctypes.c_void_p, ctypes.c_char_p):
+        return "ptr"
+    if t in (ctypes.c_float, ctypes.c_double):
+        return "float"
+    return "int"
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every binding in _lib.SIGNATURES passes as many arguments, of the same kind (pointer,
+    integer, floating point) and in the same order, as its declaration in include/vdit.h."""
+    text = re.sub(r"/\*.*?\*/", " ", (ROOT / "include" / "vdit.h").read_text(), flags=re.S)
+    decls = dict(re.findall(r"\b(vdit_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text))
+    assert set(decls) == set(_lib.SIGNATURES)
+    for name, params in decls.items():
+        c = [] if params.strip() in ("", "void") else [_c_kind(x) for x in params.split(",")]
+        py = [_py_kind(t) for t in _lib.SIGNATURES[name][1]]
+        assert c == py, f"{name}: header {c} vs ctypes {py}"
